@@ -1,0 +1,388 @@
+"""Benchmark of the fused B200 sampling step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one `UnshardedFusedSingular.autoregressive` call (fused prologue, top-128,
+top-k/top-p/min-p, Gumbel-max, logprobs) over B=64 rows of V=128256 bf16 logits with every
+logit processor enabled. `value` is rows/s over the device-timed steps (inputs resident in
+HBM, L2 flushed between steps); `e2e` times the same call with the step's logits copied from
+pinned host memory and the tokens + logprobs read back. Under torchrun each rank samples its
+own 64 rows on its own GPU (weak scaling, no collective on the data path); the timing is
+the max over ranks.
+
+`--impl reference` times the CPU restatement of the reference algorithm (oracle/) on all
+host cores on a bounded sample of the same workload; it is the reference arm of the
+comparison and never touches the GPU.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from concurrent.futures import ThreadPoolExecutor
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "sampled rows/s and HBM GB/s vs ~8 TB/s (B=64, V=128256 bf16) at 1/2/4/8 B200"
+BATCH, VOCAB = 64, 128256
+WORKLOAD = "config2: UnshardedFusedSingular.autoregressive B=64 V=128256 bf16, all processors"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.is_file():
+        return json.loads(p.read_text())
+    return {}
+
+
+def ncu_traffic() -> dict:
+    """dram bytes per launch from the committed ncu summary (profiles/), when present."""
+    out = {}
+    p = ROOT / "profiles" / "traffic.txt"
+    if p.is_file():
+        for line in p.read_text().splitlines():
+            if ":" in line and not line.lstrip().startswith("#"):
+                k, v = line.split(":", 1)
+                try:
+                    out[k.strip()] = float(v.split()[0])
+                except (ValueError, IndexError):
+                    pass
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle samples taken while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def max_over_ranks(value: float, world: int, device) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+# ------------------------------------------------------------------------------------------
+# GPU arm
+# ------------------------------------------------------------------------------------------
+
+
+def run_ours(args) -> None:
+    from sonic_sampler_b200 import _abi, roofline, workloads
+    from sonic_sampler_b200.interface import UnshardedFusedSingular
+
+    world, rank, local = dist_setup()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    _abi.load_library()
+
+    w = workloads.config2(dev, seed=1000 + rank)
+    logits, buffers = w["logits"], w["buffers"]
+    sampler = UnshardedFusedSingular.initialize(VOCAB, batch_size=BATCH)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        return sampler.autoregressive(logits, buffers, logprobs=True)
+
+    # capture one step in a CUDA graph (the deployment mode; replay costs no host work)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    clocks = ClockSampler(dev.index).start() if rank == 0 else None
+    time.sleep(0.3 if clocks else 0)
+    barrier(world)
+    for i in range(args.steps):
+        flush.fill_(i & 0xFF)  # evict the previous step's inputs from L2 (outside the timed pair)
+        starts[i].record(stream)
+        graph.replay()
+        ends[i].record(stream)
+    barrier(world)
+    clock_info = clocks.stop() if clocks else None
+    per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = max_over_ranks(sum(per_step_ms), world, dev)
+    ms_per_step = total_ms / args.steps
+    rows_per_s = world * BATCH * args.steps / (total_ms / 1e3)
+
+    # end to end: host logits in pinned memory -> device -> sampler -> tokens/logprobs to host
+    host_logits = logits.cpu().pin_memory()
+    host_tokens = torch.empty(BATCH, 1, dtype=torch.int32).pin_memory()
+    host_lp = torch.empty(BATCH, 1, dtype=torch.bfloat16).pin_memory()
+    dev_logits = torch.empty_like(logits)
+
+    def e2e_step():
+        dev_logits.copy_(host_logits, non_blocking=True)
+        sel = sampler.autoregressive(dev_logits, buffers, logprobs=True)
+        host_tokens.copy_(sel.tokens, non_blocking=True)
+        host_lp.copy_(sel.logprobs.selected, non_blocking=True)
+
+    for _ in range(3):
+        e2e_step()
+    torch.cuda.synchronize()
+    e2e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e2e_graph):
+        e2e_step()
+    for _ in range(args.warmup):
+        e2e_graph.replay()
+    e2e_steps = max(1, min(args.steps, 2000))
+    es = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    ee = [torch.cuda.Event(enable_timing=True) for _ in range(e2e_steps)]
+    barrier(world)
+    for i in range(e2e_steps):
+        flush.fill_(i & 0xFF)
+        es[i].record(stream)
+        e2e_graph.replay()
+        ee[i].record(stream)
+    barrier(world)
+    e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(es, ee)), world, dev)
+    e2e_rows = world * BATCH * e2e_steps / (e2e_ms / 1e3)
+    del graph, e2e_graph
+
+    if rank != 0:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+        return
+
+    # roofline of the fused kernel (one launch per step)
+    ind = buffers.flags.target.cpu().tolist()
+    alg_bytes = roofline.singular_call_bytes(ind, VOCAB, logprobs=True, top_z=0)
+    launch_s = (sum(per_step_ms) / args.steps) / 1e3
+    achieved = alg_bytes / launch_s / 1e9
+    peaks = measured_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    traffic = ncu_traffic().get("config2_dram_bytes_per_launch")
+
+    line = {
+        "metric": METRIC,
+        "value": round(rows_per_s, 1),
+        "unit": "rows/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 6),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded config-2 distributions: N(0,3^2)+4 peaks +12, heterogeneous params)",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": BATCH, "vocab": VOCAB,
+                   "l2": "flushed between steps (256 MiB write outside the timed events)",
+                   "parallelism": f"batch rows x{world} (weak, no collective)"},
+        "e2e": {"value": round(e2e_rows, 1), "unit": "rows/s",
+                "h2d_bytes_per_step": host_logits.numel() * host_logits.element_size(),
+                "d2h_bytes_per_step": host_tokens.numel() * 4 + host_lp.numel() * 2},
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6.65 TB/s"},
+        "clocks": clock_info,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(logits.cpu(), buffers, budget_s=args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------------------------------------------
+# CPU (reference-algorithm) arm
+# ------------------------------------------------------------------------------------------
+
+
+def _oracle_rows(logits_h, hb, rows: range):
+    """Oracle over `rows` of config 2 (rows -> slots via an explicit slot mapping)."""
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.singular import prepare_singular
+
+    sm = torch.arange(rows.start, rows.stop, dtype=torch.int32)
+    _, a = prepare_singular(
+        logits_h[rows.start:rows.stop], hb.flags.target, return_logprobs=True, block_n=4096, slot_mapping=sm,
+        grammar=hb.grammar[:, 0], context_counts=hb.repetition.counts.context,
+        decode_counts=hb.repetition.counts.decode, repetition_penalties=hb.repetition.multiplicative,
+        frequency_penalties=hb.repetition.frequency, presence_penalties=hb.repetition.presence, logit_bias=hb.bias,
+        temperature=hb.temperature, top_k=hb.top_k, top_p=hb.top_p, min_p=hb.min_p, top_k_logprobs=hb.top_logprobs,
+        gumbel_noise=hb.weights.gumbel.target[:, 0],
+    )
+    oracle.fused_singular(a)
+
+
+def cpu_baseline(logits_h, buffers, budget_s: float = 15.0, threads: int | None = None) -> dict:
+    """Time the CPU restatement on the host cores over whole batches of config 2 until about
+    `budget_s` seconds of wall time have elapsed; rows/s over the batches completed."""
+    from oracle import oracle
+
+    oracle.load()
+    hb = buffers.to("cpu") if buffers.bias.device.type != "cpu" else buffers
+    threads = threads or os.cpu_count() or 1
+    chunks = [range(i * BATCH // threads, (i + 1) * BATCH // threads) for i in range(threads)]
+    chunks = [c for c in chunks if len(c)]
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
+        while True:
+            list(pool.map(lambda c: _oracle_rows(logits_h, hb, c), chunks))
+            done += BATCH
+            if time.perf_counter() - t0 >= budget_s:
+                break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt, 1), "unit": "rows/s", "cores": len(chunks), "kind": "port",
+            "sample": f"{done // BATCH} full batches of config 2 (B=64, V=128256) in {dt:.1f} s, "
+                      f"{len(chunks)} threads over row slices"}
+
+
+def run_reference(args) -> None:
+    """Each step: one full config-2 batch (64 rows) through the CPU restatement, rows spread
+    over all host threads."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+    from sonic_sampler_b200 import workloads
+
+    oracle.load()
+    w = workloads.config2("cpu", seed=1000)
+    logits_h, hb = w["logits"], w["buffers"]
+    threads = os.cpu_count() or 1
+    chunks = [c for c in (range(i * BATCH // threads, (i + 1) * BATCH // threads) for i in range(threads)) if len(c)]
+    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
+        run = lambda: list(pool.map(lambda c: _oracle_rows(logits_h, hb, c), chunks))  # noqa: E731
+        for _ in range(args.warmup):
+            run()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            run()
+        dt = time.perf_counter() - t0
+    value = round(BATCH * args.steps / dt, 1)
+    line = {
+        "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (config 2)",
+        "config": {"workload": WORKLOAD, "rows_per_gpu": BATCH, "vocab": VOCAB},
+        "impl": "reference",
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": len(chunks), "kind": "port",
+                         "sample": f"{args.steps} full batches of config 2 (B=64, V=128256), "
+                                   f"{len(chunks)} threads over row slices"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

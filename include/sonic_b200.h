@@ -1,0 +1,233 @@
+/*
+ * sonic_b200.h -- C ABI of the B200 (sm_100a) fused sampling / speculative-verification
+ * hot path.
+ *
+ * Every entry point takes one argument struct of raw pointers, element strides and dtype
+ * tags, plus an opaque CUDA stream handle (`cudaStream_t` passed as `void*`, NULL = legacy
+ * default stream). Nothing in this header depends on PyTorch or on CUDA headers, so any FFI
+ * (ctypes, cgo, JNI, N-API) can bind it. No entry point allocates device memory: the caller
+ * passes a device workspace of at least the size the matching `*_workspace_size` query
+ * returns; the workspace must be zero-filled once before first use, and every successful
+ * call leaves its counters at zero again, so the same workspace serves any number of calls
+ * (calls that overlap on the GPU must use distinct workspaces).
+ *
+ * Calls are asynchronous (kernel launches on `stream`, no host synchronisation, no
+ * allocation), so they can be captured in a CUDA graph. Status codes never throw across
+ * the ABI; `sonic_last_error()` returns the calling thread's last message.
+ *
+ * Reference interfaces replaced (tachyontrails/sonic-sampler, paths under src/sonic_sampler/):
+ *   sonic_fused_singular   <- interface/functional/singular.py:75-322 (fused_singular:
+ *                             ops/prologue.py:272 bitpacked_reduction_kernel +
+ *                             ops/singular.py:154 cumulative_selection_kernel)
+ *   sonic_fused_multistep  <- interface/functional/multistep.py:175-461 (fused_multistep:
+ *                             ops/prologue.py:272 + ops/multistep.py:76
+ *                             cumulative_unpack_kernel + ops/verify.py:244
+ *                             chain_speculative_verification_kernel)
+ *   sonic_bounded_topk     <- interface/topk.py:98-161 (UnshardedBoundedTopK.__call__:
+ *                             ops/topk/bitpack.py:99 + ops/topk/unpack.py:312)
+ */
+#ifndef SONIC_B200_H
+#define SONIC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SONIC_B200_ABI_VERSION 1
+
+/* Candidate-set width of the two-stage top-k (reference ops/base.py:24, MAX_K). */
+#define SONIC_MAX_K 128
+/* Largest speculation lookahead gamma accepted by sonic_fused_multistep / drafting. */
+#define SONIC_MAX_LOOKAHEAD 15
+
+typedef int32_t sonic_status;
+enum {
+  SONIC_OK = 0,
+  SONIC_ERR_INVALID_ARGUMENT = 1, /* bad shape, stride, dtype, null pointer or flag */
+  SONIC_ERR_UNSUPPORTED = 2,      /* valid request this build does not implement */
+  SONIC_ERR_WORKSPACE = 3,        /* workspace missing or smaller than required */
+  SONIC_ERR_CUDA = 4              /* a CUDA runtime call failed (message has details) */
+};
+
+enum {
+  SONIC_DTYPE_BF16 = 0,
+  SONIC_DTYPE_F32 = 1,
+  SONIC_DTYPE_I32 = 2,
+  SONIC_DTYPE_I64 = 3
+};
+
+/* Call flags (bit set in the `flags` field of each argument struct). */
+enum {
+  SONIC_FLAG_PDL = 1u << 0,            /* launch with programmatic dependent launch */
+  SONIC_FLAG_PREFILL = 1u << 1,        /* decode-count update writes 1 instead of +1 */
+  SONIC_FLAG_UPDATE_COUNTS = 1u << 2,  /* update decode counts with the selected tokens */
+  SONIC_FLAG_LOGPROBS = 1u << 3,       /* write selected (and top-Z) logprobs */
+  SONIC_FLAG_PROBABILITIES = 1u << 4,  /* singular: write candidate probabilities */
+  SONIC_FLAG_PHILOX = 1u << 5          /* singular: counter-based Philox Gumbel noise */
+};
+
+/*
+ * Per-request sampling parameters: the device-resident fields of the reference's
+ * SamplingBuffers (core/buffer.py:784-817, core/flags.py:435-521). All are indexed by the
+ * request slot (after slot indirection). Any pointer may be NULL when no row's indicator
+ * needs it (the reference passes None the same way).
+ */
+typedef struct SonicSamplingParams {
+  const uint16_t* indicators;     /* u16 [slots]: Indicator bit field (core/flags.py:58-95) */
+  const void* slot_mapping;       /* [requests] i32 or i64, or NULL (identity) */
+  int32_t slot_dtype;             /* SONIC_DTYPE_I32 / SONIC_DTYPE_I64 */
+  int32_t num_slots;              /* rows of the per-slot buffers (bounds checks only) */
+  const uint32_t* grammar;        /* u32 bit mask words, row (slot*timesteps+step) */
+  int64_t grammar_stride;         /* words between consecutive grammar rows */
+  const int32_t* context_counts;  /* i32 [slots, counts_stride] */
+  int32_t* decode_counts;         /* i32 [slots, counts_stride] (updated in place) */
+  int64_t counts_stride;          /* elements between count rows */
+  const uint16_t* repetition;     /* bf16 [slots] multiplicative penalty */
+  const uint16_t* frequency;      /* bf16 [slots] */
+  const uint16_t* presence;       /* bf16 [slots] */
+  const uint16_t* bias;           /* bf16 [slots, bias_stride] */
+  int64_t bias_stride;            /* elements between bias rows */
+  const uint16_t* temperature;    /* bf16 [slots] */
+  const int32_t* top_k;           /* i32 [slots] */
+  const uint16_t* top_p;          /* bf16 [slots] */
+  const uint16_t* min_p;          /* bf16 [slots] */
+  const int32_t* top_logprobs;    /* i32 [slots] number of top-Z logprobs requested */
+} SonicSamplingParams;
+
+/*
+ * One-token selection per row (autoregressive decode or drafting step).
+ * Replaces reference interface/functional/singular.py:75 fused_singular.
+ */
+typedef struct SonicSingularArgs {
+  int32_t rows;              /* R logits rows */
+  int32_t vocab_size;        /* columns sampled (local vocab) */
+  int32_t block_n;           /* reference tile width: fixes the greedy tie rule */
+  int32_t lookahead;         /* gamma: drafted-token columns counted (drafting, t > 0) */
+  int32_t shard_offset;      /* added to columns before aux-buffer lookups */
+  int32_t max_top_logprobs;  /* Z capacity of the top-logprob outputs */
+  int32_t target_vocab;      /* row length of `probabilities` (bounds checks only) */
+  uint32_t flags;            /* SONIC_FLAG_* */
+
+  const void* logits;        /* [R, logits_stride] bf16 */
+  int32_t logits_dtype;      /* SONIC_DTYPE_BF16 */
+  int64_t logits_stride;
+
+  SonicSamplingParams params;
+
+  const void* d2t;           /* [vocab] draft->target id table (i32/i64) or NULL */
+  int32_t d2t_dtype;
+  const int32_t* drafted_tokens; /* [slots, drafted_stride] drafted ids or NULL */
+  int64_t drafted_stride;
+
+  const uint16_t* gumbel;    /* bf16 log(Exp(1)) noise, [slots, gumbel_stride] */
+  int64_t gumbel_stride;
+  uint64_t philox_seed;      /* SONIC_FLAG_PHILOX: key of the counter-based noise */
+  uint64_t philox_offset;    /* SONIC_FLAG_PHILOX: per-call counter offset */
+
+  int32_t* tokens;           /* out i32 [R] at tokens[r*tokens_stride] */
+  int64_t tokens_stride;
+  void* logprobs;            /* out [R] at logprobs[r*logprobs_stride] or NULL */
+  int64_t logprobs_stride;
+  int32_t logprobs_dtype;    /* SONIC_DTYPE_BF16 (reference) or SONIC_DTYPE_F32 */
+  void* top_logprob_values;  /* out [R, top_stride] (logprobs_dtype) or NULL */
+  int32_t* top_logprob_tokens;  /* out i32 [R, top_stride] or NULL */
+  int64_t top_stride;
+  void* probabilities;       /* out [slots, probabilities_stride] bf16/f32 or NULL */
+  int32_t probabilities_dtype;
+  int64_t probabilities_stride;
+
+  void* workspace;           /* device scratch, zero-filled before first use */
+  size_t workspace_bytes;
+} SonicSingularArgs;
+
+/*
+ * Multi-step target verification of gamma drafted tokens per request.
+ * Replaces reference interface/functional/multistep.py:175 fused_multistep.
+ */
+typedef struct SonicMultistepArgs {
+  int32_t batch_size;        /* B requests */
+  int32_t lookahead;         /* gamma (maximum, for varlen) */
+  int32_t vocab_size;
+  int32_t block_n;           /* reference tile width: fixes the greedy tie rule */
+  int32_t shard_offset;
+  int32_t max_top_logprobs;
+  uint32_t flags;            /* SONIC_FLAG_PDL / _UPDATE_COUNTS / _LOGPROBS */
+  int32_t total_rows;        /* L = B*(gamma+1), or cu_seqlens[B] for varlen */
+
+  const void* logits;        /* [L, logits_stride] bf16 */
+  int32_t logits_dtype;
+  int64_t logits_stride;
+  const int32_t* cu_seqlens; /* [B+1] row offsets (varlen) or NULL */
+
+  SonicSamplingParams params;
+
+  const int32_t* drafted_tokens; /* flat [L]: request b's draft ids at margin_b + s */
+  const void* draft_probs;   /* q: [slots, draft_stride] rows, step stride draft_step_stride */
+  int32_t draft_dtype;       /* SONIC_DTYPE_F32 / SONIC_DTYPE_BF16 */
+  int64_t draft_stride;
+  int64_t draft_step_stride;
+  const uint16_t* uniform;   /* bf16 [slots, uniform_stride] acceptance draws */
+  int64_t uniform_stride;
+  const uint16_t* gumbel;    /* bf16 [slots, gumbel_stride], step stride gumbel_step_stride */
+  int64_t gumbel_stride;
+  int64_t gumbel_step_stride;
+
+  float* values;             /* out f32 [L, 128] candidate probabilities or NULL */
+  int32_t* indices;          /* out i32 [L, 128] candidate ids or NULL */
+  int32_t* tokens;           /* out i32 flat [L]: tokens[margin_b + accepted_b] = token */
+  int32_t* offsets;          /* out i32 [B] accepted counts */
+  void* logprobs;            /* out flat [L] or NULL */
+  int32_t logprobs_dtype;    /* SONIC_DTYPE_BF16 (reference) or SONIC_DTYPE_F32 */
+  void* top_logprob_values;  /* out [L, top_stride] (logprobs_dtype) or NULL */
+  int32_t* top_logprob_tokens;  /* out i32 [L, top_stride] or NULL */
+  int64_t top_stride;
+
+  void* workspace;
+  size_t workspace_bytes;
+} SonicMultistepArgs;
+
+/*
+ * Bounded top-k (k a power of two <= 128) over each row, values descending, ties by the
+ * lowest column. Row r's k results land at values[r*k + i] / indices[r*k + i] (the
+ * reference's flat layout, interface/topk.py:117-159 with ops/topk/unpack.py:374-377).
+ * Replaces reference interface/topk.py:98 UnshardedBoundedTopK.__call__.
+ */
+typedef struct SonicTopKArgs {
+  int32_t rows;
+  int32_t vocab_size;
+  int32_t k;
+  int32_t block_n;           /* accepted for interface parity; no effect on results */
+  uint32_t flags;            /* SONIC_FLAG_PDL */
+  const void* logits;        /* [rows, logits_stride] bf16 or f32 */
+  int32_t logits_dtype;
+  int64_t logits_stride;
+  void* values;              /* out: bf16 (bf16 logits) or f32 (f32 logits) */
+  int32_t values_dtype;
+  void* indices;             /* out: i32 or i64 */
+  int32_t indices_dtype;
+  void* workspace;
+  size_t workspace_bytes;
+} SonicTopKArgs;
+
+/* Device workspace (bytes) a call with these arguments needs. Only shape fields are read. */
+size_t sonic_fused_singular_workspace_size(const SonicSingularArgs* args);
+size_t sonic_fused_multistep_workspace_size(const SonicMultistepArgs* args);
+size_t sonic_bounded_topk_workspace_size(const SonicTopKArgs* args);
+
+sonic_status sonic_fused_singular(const SonicSingularArgs* args, void* stream);
+sonic_status sonic_fused_multistep(const SonicMultistepArgs* args, void* stream);
+sonic_status sonic_bounded_topk(const SonicTopKArgs* args, void* stream);
+
+/* ABI version (SONIC_B200_ABI_VERSION) the library was built with. */
+int32_t sonic_abi_version(void);
+/* Message of the calling thread's last failed call ("" when none). */
+const char* sonic_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SONIC_B200_H */

@@ -1,0 +1,118 @@
+"""The C-ABI library loads on a machine without a GPU, exports exactly what
+include/sonic_b200.h declares, and validates arguments on the host before any launch."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from sonic_sampler_b200 import _abi
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "sonic_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from sonic_sampler_b200 import build
+
+    build.build()
+    return _abi.load_library()
+
+
+def declared_functions() -> set[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return set(re.findall(r"\b(sonic_\w+)\s*\(", text))
+
+
+def test_header_declares_the_python_mirror():
+    assert declared_functions() == set(_abi.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_abi.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert exported == declared_functions()
+    for name in declared_functions():
+        assert hasattr(lib, name)
+
+
+def test_abi_version(lib):
+    assert lib.sonic_abi_version() == _abi.ABI_VERSION
+
+
+def test_struct_layout_matches_header():
+    """The ctypes mirror names every field of the header's structs in header order."""
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    for cname, pyt in (("SonicSamplingParams", _abi.SamplingParams), ("SonicSingularArgs", _abi.SingularArgs),
+                       ("SonicMultistepArgs", _abi.MultistepArgs), ("SonicTopKArgs", _abi.TopKArgs)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
+        fields = []
+        for decl in body.split(";"):
+            decl = decl.strip()
+            if not decl:
+                continue
+            fields.append(re.findall(r"(\w+)\s*$", decl)[0])
+        assert fields == [f for f, _ in pyt._fields_], cname
+
+
+def test_workspace_queries_are_pure(lib):
+    a = _abi.SingularArgs()
+    a.rows, a.vocab_size = 64, 128256
+    n1 = lib.sonic_fused_singular_workspace_size(ctypes.byref(a))
+    n2 = lib.sonic_fused_singular_workspace_size(ctypes.byref(a))
+    assert n1 == n2 > 64 * 128 * 8
+    m = _abi.MultistepArgs()
+    m.batch_size, m.lookahead, m.vocab_size = 32, 4, 128256
+    assert lib.sonic_fused_multistep_workspace_size(ctypes.byref(m)) > 32 * 5 * 128 * 8
+    t = _abi.TopKArgs()
+    t.rows, t.vocab_size = 8, 32000
+    assert lib.sonic_bounded_topk_workspace_size(ctypes.byref(t)) > 0
+    assert lib.sonic_fused_singular_workspace_size(None) == 0
+
+
+def _status(lib, fn, args):
+    return getattr(lib, fn)(ctypes.byref(args), None), lib.sonic_last_error().decode()
+
+
+def test_host_validation_without_gpu(lib):
+    """Bad arguments are rejected before any CUDA call (so these run on CPU machines)."""
+    a = _abi.SingularArgs()
+    a.rows, a.vocab_size, a.block_n = 4, 1000, 1000
+    st, msg = _status(lib, "sonic_fused_singular", a)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "block_n" in msg
+    a.block_n = 1024
+    st, msg = _status(lib, "sonic_fused_singular", a)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "indicators" in msg
+    a.vocab_size = 64
+    st, msg = _status(lib, "sonic_fused_singular", a)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "vocab_size" in msg
+    a.rows = 0
+    assert _status(lib, "sonic_fused_singular", a)[0] == _abi.SONIC_OK  # empty batch: no-op
+
+    m = _abi.MultistepArgs()
+    m.batch_size, m.lookahead, m.vocab_size, m.block_n = 2, 16, 4096, 1024
+    st, msg = _status(lib, "sonic_fused_multistep", m)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "lookahead" in msg
+
+    t = _abi.TopKArgs()
+    t.rows, t.vocab_size, t.k = 2, 4096, 48
+    st, msg = _status(lib, "sonic_bounded_topk", t)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "power of two" in msg
+
+
+def test_update_counts_without_decode_counts_message(lib):
+    """Same message as the reference's runtime check (functional/base.py:34-38)."""
+    import torch
+
+    from sonic_sampler_b200.interface.functional.singular import prepare_singular
+
+    with pytest.raises(ValueError, match="`update_counts` is True but `decode_counts` is None"):
+        prepare_singular(torch.zeros(2, 4096, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.uint16),
+                         update_counts=True)
