@@ -2,13 +2,16 @@
 // include/sonic_b200.h.
 //
 // One launch per call. Each row (singular, top-k) or request (multistep) is cut into S
-// column splits; one 256-thread CTA streams one split from HBM exactly once with 16-byte
-// vector loads, applies the reference logit processors in registers, and keeps a
-// shared-memory candidate buffer behind a rising value threshold, so most logits cost a
-// load, a few bf16 ops and one compare. The split's exact top-128 (or, for greedy rows,
-// its single best key) is written sorted to the workspace; the last CTA of the row or
-// request to finish (per-row ticket in the workspace) merges the S sorted lists with warp
-// bitonic merges and runs selection / verification. No second launch, no host sync.
+// column splits, one 256-thread CTA per split. A CTA streams its split from HBM exactly
+// once: bulk (TMA) copies fill a 3-stage shared-memory ring that is refilled as soon as a
+// stage is consumed, so two chunks are always in flight. Each thread turns 8 columns into
+// processed bf16 logits with packed bf16x2 arithmetic and keeps the ones at or above a
+// rising value threshold: single-row kernels in a sorted per-warp top-128 held in
+// registers (fed through a per-warp shared-memory queue), the multistep kernel in a
+// per-row shared-memory candidate buffer. The split's exact top-128 (or, for greedy
+// rows, its single best key) goes to the workspace, sorted. The last CTA
+// of the row or request (per-unit ticket in the workspace) merges the S sorted lists with
+// warp bitonic merges and runs selection / verification. No second launch, no host sync.
 //
 // Reference kernels covered (tachyontrails/sonic-sampler, src/sonic_sampler/):
 //   ops/prologue.py:272-472   bitpacked_reduction_kernel (processors + tile candidates)
@@ -31,28 +34,35 @@
 
 namespace sonic {
 
-constexpr int NT = 256;           // threads per CTA
-constexpr int VPT = 8;            // consecutive columns per thread per chunk (16 B of bf16)
-constexpr int CHUNK = NT * VPT;   // columns per CTA per chunk
-constexpr int CAP = 4096;         // candidate buffer (keys) for single-row CTAs
-constexpr int TARGET_CTAS = 592;  // 148 SMs x 4 resident CTAs
-constexpr int MAX_SPLIT_COLS = 65536;
+constexpr int NT = 256;                    // threads per CTA
+constexpr int VPT = 8;                     // consecutive columns per thread per chunk
+constexpr int CH = NT * VPT;               // columns per chunk (single-row kernels)
+constexpr int CH_MS = 1024;                // columns per chunk (multistep: many rows per CTA)
+constexpr int VPT_MS = CH_MS / NT;         // 4 columns per thread (multistep)
+constexpr int STAGES = 3;                  // bulk-copy ring depth
+constexpr int CAP_MS = 1536;               // candidate keys per row of a multistep CTA
+constexpr int TARGET_CTAS = 296;           // 148 SMs x 2 resident CTAs: one wave
+constexpr int MAX_SPLIT_COLS = 65536;      // local column index fits 16 bits
 constexpr int MAX_SPLITS = 32;
+constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls of a bulk-copy barrier before giving up
+constexpr int MS_MAX_STEPS = SONIC_MAX_LOOKAHEAD + 1;
+
+enum LoadMode { kTma = 0, kVec = 1, kScalar = 2 };
 
 struct Plan {
   int splits;
   int cols;
 };
 
-// Column split of a unit (row or request) of V columns; a pure function of the shapes so
+// Column split of a unit (row or request) of V columns; a pure function of the shapes, so
 // the workspace size never depends on the device.
-static Plan split_plan(int64_t units, int64_t V) {
-  int64_t s = units > 0 ? (TARGET_CTAS + units - 1) / units : 1;
+static Plan split_plan(int64_t units, int64_t V, int chunk) {
+  int64_t s = units > 0 ? TARGET_CTAS / units : 1;
+  s = std::max<int64_t>(s, 1);
   s = std::max<int64_t>(s, (V + MAX_SPLIT_COLS - 1) / MAX_SPLIT_COLS);
   s = std::min<int64_t>(s, MAX_SPLITS);
-  s = std::max<int64_t>(s, 1);
   int64_t cols = (V + s - 1) / s;
-  cols = (cols + CHUNK - 1) / CHUNK * CHUNK;
+  cols = (cols + chunk - 1) / chunk * chunk;
   cols = std::min<int64_t>(cols, MAX_SPLIT_COLS);
   Plan p;
   p.splits = (int)((V + cols - 1) / cols);
@@ -60,13 +70,26 @@ static Plan split_plan(int64_t units, int64_t V) {
   return p;
 }
 
-// workspace: [units][splits][128] u64 sorted candidate keys, then [units] u32 tickets.
-static size_t workspace_bytes(int64_t units, int64_t V) {
+// workspace: [rows][splits][128] u64 sorted candidate keys | [units] u32 tickets | u32 error
+struct Workspace {
+  uint64_t* cand;
+  uint32_t* tickets;
+  uint32_t* error;
+};
+
+static size_t workspace_bytes(int64_t rows, int64_t units, int64_t splits) {
   if (units <= 0) return 0;
-  Plan p = split_plan(units, V);
-  size_t cand = (size_t)units * p.splits * kMaxK * sizeof(uint64_t);
-  size_t tick = (size_t)units * sizeof(uint32_t);
-  return cand + ((tick + 255) / 256) * 256;
+  const size_t cand = (size_t)rows * splits * kMaxK * sizeof(uint64_t);
+  const size_t tick = ((size_t)units * sizeof(uint32_t) + 4 + 255) / 256 * 256;
+  return cand + tick;
+}
+
+static Workspace carve(void* base, int64_t rows, int64_t units, int64_t splits) {
+  Workspace w;
+  w.cand = (uint64_t*)base;
+  w.tickets = (uint32_t*)((char*)base + (size_t)rows * splits * kMaxK * sizeof(uint64_t));
+  w.error = w.tickets + units;
+  return w;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -74,9 +97,7 @@ static size_t workspace_bytes(int64_t units, int64_t V) {
 // ---------------------------------------------------------------------------------------
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_trigger() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ int64_t load_index(const void* p, int32_t dtype, int64_t i) {
   return dtype == SONIC_DTYPE_I64 ? ((const int64_t*)p)[i] : (int64_t)((const int32_t*)p)[i];
@@ -86,22 +107,21 @@ __device__ __forceinline__ uint64_t ldcg64(const uint64_t* p) {
   return (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(p));
 }
 
-__device__ __forceinline__ uint4 ld_stream(const void* p) {
-  return __ldcs(reinterpret_cast<const uint4*>(p));
+__device__ __forceinline__ void stcg64(uint64_t* p, uint64_t v) {
+  __stcg(reinterpret_cast<unsigned long long*>(p), (unsigned long long)v);
 }
 
-struct RowParams {
-  float rep, freq, pres, temp;
-};
+__device__ __forceinline__ uint4 ld_stream(const void* p) { return __ldcs(reinterpret_cast<const uint4*>(p)); }
 
-__device__ __forceinline__ RowParams load_row_params(const SonicSamplingParams& P, int64_t slot,
-                                                     uint32_t ind) {
-  RowParams rp;
-  rp.rep = (P.repetition && (ind & 0x2)) ? bf2f(P.repetition[slot]) : 1.0f;
-  rp.freq = (P.frequency && (ind & 0x4)) ? bf2f(P.frequency[slot]) : 0.0f;
-  rp.pres = (P.presence && (ind & 0x8)) ? bf2f(P.presence[slot]) : 0.0f;
-  rp.temp = (P.temperature && (ind & 0x20)) ? bf2f(P.temperature[slot]) : 1.0f;
-  return rp;
+__device__ __forceinline__ void store_float(void* base, int32_t dtype, int64_t i, float x) {
+  if (dtype == SONIC_DTYPE_F32)
+    ((float*)base)[i] = x;
+  else
+    ((uint16_t*)base)[i] = f2bf(x);
+}
+
+__device__ __forceinline__ int64_t load_slot(const SonicSamplingParams& P, int64_t unit) {
+  return P.slot_mapping ? load_index(P.slot_mapping, P.slot_dtype, unit) : unit;
 }
 
 // Which aux streams a row needs (reference ops/prologue.py:378-447).
@@ -109,43 +129,170 @@ struct Needs {
   bool proc, g, dec, ctx, bias, temp;
 };
 
-__device__ __forceinline__ Needs row_needs(const SonicSamplingParams& P, uint32_t ind) {
-  Needs n;
+// Per-row constants of the logit processors.
+struct RowConsts {
+  uint32_t ind;
+  Needs nd;
+  float rep, rrep;        // multiplicative penalty and RN(1/penalty)
+  bool rep_fast;          // v / rep == v * rrep after bf16 rounding (penalty in [2^-8, 2^8])
+  uint32_t freq2, pres2;  // bf16 penalties in both halves
+  float temp, rtemp;
+  bool temp_fast;
+  bool fast;  // stochastic row whose final value is a monotone map of the post-bias value
+  bool decr;  // fast row whose penalties never raise a logit (given non-negative counts)
+};
+
+// For bf16 v and a bf16 divisor t in [2^-8, 2^8], bf16(v / t) == bf16(v * RN(1/t)): the exact
+// quotient of two 8-bit significands is never within 2^-16 (relative) of a bf16 rounding
+// midpoint, far above the 2-ulp fp32 error of the reciprocal product (checked exhaustively
+// over all bf16 v and t in that range).
+__device__ __forceinline__ bool recip_exact_range(float t) { return t >= 0.00390625f && t <= 256.0f; }
+
+__device__ __forceinline__ RowConsts row_consts(const SonicSamplingParams& P, int64_t slot, uint32_t ind) {
+  RowConsts rc;
+  rc.ind = ind;
+  Needs& n = rc.nd;
   n.proc = (ind & 0x1F) != 0;
   n.g = n.proc && P.grammar && (ind & 0x1);
   n.dec = n.proc && P.decode_counts && (ind & 0xE);
   n.ctx = n.dec && P.context_counts && (ind & 0x2);
   n.bias = n.proc && P.bias && (ind & 0x10);
   n.temp = (ind & 0x20) != 0;
-  return n;
+  rc.rep = (n.ctx && P.repetition) ? bf2f(P.repetition[slot]) : 1.0f;
+  rc.rrep = __frcp_rn(rc.rep);
+  rc.rep_fast = recip_exact_range(rc.rep);
+  const uint32_t f = (P.frequency && (ind & 0x4)) ? P.frequency[slot] : 0u;
+  const uint32_t p = (P.presence && (ind & 0x8)) ? P.presence[slot] : 0u;
+  rc.freq2 = f | (f << 16);
+  rc.pres2 = p | (p << 16);
+  rc.temp = (P.temperature && n.temp) ? bf2f(P.temperature[slot]) : 1.0f;
+  rc.rtemp = __frcp_rn(rc.temp);
+  rc.temp_fast = recip_exact_range(rc.temp);
+  // The fast path skips the penalties where both counts are zero; that is exact unless a
+  // negative frequency / presence penalty turns a -0.0 logit into +0.0.
+  const bool neg_pen = n.dec && (((ind & 0x4) && (f & 0x8000u)) || ((ind & 0x8) && (p & 0x8000u)));
+  const bool temp_ok = !n.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f);
+  rc.fast = !(ind & 0x40) && !neg_pen && temp_ok;
+  rc.decr = rc.fast && (!n.ctx || rc.rep >= 1.0f);
+  return rc;
 }
 
-// The reference logit processors for one logit (ops/prologue.py:29-114, 443-447), in its
-// order and with its bf16 rounding after every operation.
-__device__ __forceinline__ float apply_processors(float v, uint32_t ind, const Needs& n, bool gbit,
-                                                  int32_t dec, int32_t ctx, float bias,
-                                                  const RowParams& rp) {
-  if (n.proc) {
-    if (n.g && !gbit) v = __int_as_float(0xff800000);
-    if (n.dec) {
-      if (n.ctx) {
-        const int32_t total = dec + ctx;
-        const float s = total > 0 ? rp.rep : 1.0f;
-        v = v < 0.0f ? rbf(__fmul_rn(v, s)) : rbf(__fdiv_rn(v, s));
-      }
-      if (ind & 0x4) v = rbf(__fsub_rn(v, rbf(__fmul_rn(rbf(__int2float_rn(dec)), rp.freq))));
-      if (ind & 0x8) v = rbf(__fsub_rn(v, rbf(__fmul_rn(dec > 0 ? 1.0f : 0.0f, rp.pres))));
+__device__ __forceinline__ float penalize(float v, bool seen, const RowConsts& rc) {
+  if (!seen) return v;
+  if (v < 0.0f) return __fmul_rn(v, rc.rep);
+  return rc.rep_fast ? __fmul_rn(v, rc.rrep) : __fdiv_rn(v, rc.rep);
+}
+
+// The reference logit processors for two adjacent logits (ops/prologue.py:29-114, 443-447),
+// in its order, rounding to bf16 after every operation. `g2` holds the two grammar bits.
+__device__ __forceinline__ uint32_t process_pair(uint32_t x, uint32_t g2, int32_t d0, int32_t d1, int32_t c0,
+                                                 int32_t c1, uint32_t b2, const RowConsts& rc) {
+  if (rc.nd.proc) {
+    if (rc.nd.g) {
+      const uint32_t keep = ((g2 & 1u) ? 0x0000ffffu : 0u) | ((g2 & 2u) ? 0xffff0000u : 0u);
+      x = (x & keep) | (0xff80ff80u & ~keep);
     }
-    if (n.bias) v = rbf(__fadd_rn(v, bias));
+    if (rc.nd.dec) {
+      if (rc.nd.ctx) {
+        const float lo = penalize(bf2_lo(x), d0 + c0 > 0, rc);
+        const float hi = penalize(bf2_hi(x), d1 + c1 > 0, rc);
+        x = bf2_pack(lo, hi);
+      }
+      if (rc.ind & 0x4) x = bf2_sub(x, bf2_mul(bf2_pack(__int2float_rn(d0), __int2float_rn(d1)), rc.freq2));
+      if (rc.ind & 0x8) {
+        // (decode > 0) * presence: the penalty itself, or a zero carrying its sign
+        const uint32_t sel = ((d0 > 0) ? (rc.pres2 & 0x0000ffffu) : (rc.pres2 & 0x00008000u)) |
+                             ((d1 > 0) ? (rc.pres2 & 0xffff0000u) : (rc.pres2 & 0x80000000u));
+        x = bf2_sub(x, sel);
+      }
+    }
+    if (rc.nd.bias) x = bf2_add(x, b2);
   }
-  if (n.temp) v = rbf(__fdiv_rn(v, rp.temp));
-  return v;
+  if (rc.nd.temp) {
+    float lo = bf2_lo(x), hi = bf2_hi(x);
+    if (rc.temp_fast) {
+      lo = __fmul_rn(lo, rc.rtemp);
+      hi = __fmul_rn(hi, rc.rtemp);
+    } else {
+      lo = __fdiv_rn(lo, rc.temp);
+      hi = __fdiv_rn(hi, rc.temp);
+    }
+    x = bf2_pack(lo, hi);
+  }
+  return x;
+}
+
+// Raw inputs of 8 consecutive columns.
+struct Raw8 {
+  uint32_t x[4];   // bf16 pairs
+  int32_t d[VPT];  // decode counts
+  int32_t c[VPT];  // context counts
+  uint32_t b[4];   // bias pairs
+  uint32_t g;      // grammar bits (bit j = column j)
+};
+
+__device__ __forceinline__ void process8(Raw8& r, const RowConsts& rc) {
+#pragma unroll
+  for (int p = 0; p < 4; ++p)
+    r.x[p] = process_pair(r.x[p], (r.g >> (2 * p)) & 3u, r.d[2 * p], r.d[2 * p + 1], r.c[2 * p], r.c[2 * p + 1],
+                          r.b[p], rc);
+}
+
+// ---------------------------------------------------------------------------------------
+// fast path of stochastic rows: penalties only where a count is nonzero (they are the
+// identity elsewhere), temperature only for candidates (it is monotone, so the candidate
+// test runs against the pre-temperature cut `vmin`), grammar as a mask bit
+// ---------------------------------------------------------------------------------------
+
+// final (post-temperature) value of a post-bias logit
+__device__ __forceinline__ float temper(float v, bool on, bool fast, float t, float rt) {
+  if (!on) return v;
+  return rbf(fast ? __fmul_rn(v, rt) : __fdiv_rn(v, t));
+}
+
+__device__ __forceinline__ float final_value(float v, const RowConsts& rc) {
+  return temper(v, rc.nd.temp, rc.temp_fast, rc.temp, rc.rtemp);
+}
+
+// multiplicative, frequency and presence penalties of one logit (ops/prologue.py:57-102)
+__device__ __forceinline__ uint32_t repetition_one(uint32_t h, int32_t d, int32_t c, const RowConsts& rc) {
+  float v = bf2f((uint16_t)h);
+  if (rc.nd.ctx) v = rbf(penalize(v, d + c > 0, rc));
+  if (rc.ind & 0x4) v = rbf(__fsub_rn(v, rbf(__fmul_rn(rbf(__int2float_rn(d)), bf2f((uint16_t)(rc.freq2 & 0xffffu))))));
+  if (rc.ind & 0x8) v = rbf(__fsub_rn(v, bf2f((uint16_t)((d > 0) ? (rc.pres2 & 0xffffu) : (rc.pres2 & 0x8000u)))));
+  return f2bf(v);
+}
+
+// 8-bit mask of the bf16 logits of x[0..3] that are >= the pair v2 (NaN never passes)
+__device__ __forceinline__ uint32_t ge_mask8(const uint32_t (&x)[4], uint32_t v2) {
+  uint32_t bits = 0;
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    const uint32_t m = __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&x[p]),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&v2));
+    bits |= (m & 0x00010001u) << (2 * p);
+  }
+  return (bits | (bits >> 15)) & 0xffu;
+}
+
+__device__ __forceinline__ uint32_t ge_mask4(const uint32_t (&x)[2], uint32_t v2) {
+  uint32_t bits = 0;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const uint32_t m = __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&x[p]),
+                                   *reinterpret_cast<const __nv_bfloat162*>(&v2));
+    bits |= (m & 0x00010001u) << (2 * p);
+  }
+  return (bits | (bits >> 15)) & 0xfu;
+}
+
+__device__ __forceinline__ uint32_t half_of(const uint32_t* x, int j) {
+  return (j & 1) ? (x[j >> 1] >> 16) : (x[j >> 1] & 0xffffu);
 }
 
 // Greedy order key (ops/prologue.py:117-138 + ops/singular.py:71-131): value, then the
 // lowest offset inside its block_n tile, then the lowest tile. -0.0 compares as +0.0.
-__device__ __forceinline__ uint64_t greedy_key(float v, int64_t c, int log2bn) {
-  uint32_t h = f2bf(v);
+__device__ __forceinline__ uint64_t greedy_key_bits(uint32_t h, int64_t c, int log2bn) {
   if (h == 0x8000u) h = 0;
   const uint64_t e = enc16(h);
   const int64_t bn = 1ll << log2bn;
@@ -161,103 +308,74 @@ __device__ __forceinline__ int64_t greedy_col(uint64_t key, int log2bn) {
 }
 
 // ---------------------------------------------------------------------------------------
-// per-thread chunk loading: 8 consecutive columns c..c+7 of one row
+// direct (non-bulk) loads of 8 columns: vector loads when aligned, else scalar / gathered
 // ---------------------------------------------------------------------------------------
 
-struct Aux8 {
-  int32_t dec[VPT];
-  int32_t ctx[VPT];
-  float bias[VPT];
-};
-
-// aux-buffer columns of the 8 logits (shard offset, optional d2t remap)
-struct Cols8 {
-  int64_t col[VPT];
-};
-
-template <bool VEC>
-__device__ __forceinline__ void load_logits8(const uint16_t* xrow, int64_t c, int nvalid,
-                                             float (&x)[VPT]) {
-  if (VEC && nvalid == VPT) {
-    uint4 q = ld_stream(xrow + c);
-    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[2 * i] = __uint_as_float(w[i] << 16);
-      x[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-    }
+template <int MODE>
+__device__ __forceinline__ void load_x8(const uint16_t* xrow, int64_t c, int nvalid, uint32_t (&x)[4]) {
+  if (MODE != kScalar && nvalid == VPT) {
+    const uint4 q = ld_stream(xrow + c);
+    x[0] = q.x;
+    x[1] = q.y;
+    x[2] = q.z;
+    x[3] = q.w;
   } else {
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) x[j] = j < nvalid ? bf2f(__ldcs(xrow + c + j)) : 0.0f;
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t lo = (2 * p < nvalid) ? (uint32_t)__ldcs(xrow + c + 2 * p) : 0xff80u;
+      const uint32_t hi = (2 * p + 1 < nvalid) ? (uint32_t)__ldcs(xrow + c + 2 * p + 1) : 0xff80u;
+      x[p] = lo | (hi << 16);
+    }
   }
 }
 
-template <bool VEC>
-__device__ __forceinline__ void load_logits8_f32(const float* xrow, int64_t c, int nvalid,
-                                                 float (&x)[VPT]) {
-  if (VEC && nvalid == VPT) {
-    uint4 a = ld_stream(xrow + c), b = ld_stream(xrow + c + 4);
-    x[0] = __uint_as_float(a.x); x[1] = __uint_as_float(a.y);
-    x[2] = __uint_as_float(a.z); x[3] = __uint_as_float(a.w);
-    x[4] = __uint_as_float(b.x); x[5] = __uint_as_float(b.y);
-    x[6] = __uint_as_float(b.z); x[7] = __uint_as_float(b.w);
-  } else {
-#pragma unroll
-    for (int j = 0; j < VPT; ++j) x[j] = j < nvalid ? __ldcs(xrow + c + j) : 0.0f;
-  }
-}
-
-// VEC: the 8 aux columns are contiguous and 32-byte aligned (checked on the host).
-template <bool VEC>
-__device__ __forceinline__ void load_aux8(const SonicSamplingParams& P, const Needs& n, int64_t slot,
-                                          const Cols8& cc, int nvalid, Aux8& a) {
-  if (VEC && nvalid == VPT) {
-    const int64_t c = cc.col[0];
-    if (n.dec) {
-      const int32_t* d = P.decode_counts + slot * P.counts_stride + c;
-      uint4 p = ld_stream(d), q = ld_stream(d + 4);
-      a.dec[0] = p.x; a.dec[1] = p.y; a.dec[2] = p.z; a.dec[3] = p.w;
-      a.dec[4] = q.x; a.dec[5] = q.y; a.dec[6] = q.z; a.dec[7] = q.w;
+// Aux values of 8 columns; `col[j]` are the aux-buffer columns (shard offset / d2t applied).
+template <int MODE>
+__device__ __forceinline__ void load_aux8(const SonicSamplingParams& P, const RowConsts& rc, int64_t slot,
+                                          const int64_t (&col)[VPT], int nvalid, Raw8& r) {
+  if (MODE != kScalar && nvalid == VPT) {
+    if (rc.nd.dec) {
+      const int32_t* d = P.decode_counts + slot * P.counts_stride + col[0];
+      const uint4 p = ld_stream(d), q = ld_stream(d + 4);
+      r.d[0] = p.x; r.d[1] = p.y; r.d[2] = p.z; r.d[3] = p.w;
+      r.d[4] = q.x; r.d[5] = q.y; r.d[6] = q.z; r.d[7] = q.w;
     }
-    if (n.ctx) {
-      const int32_t* d = P.context_counts + slot * P.counts_stride + c;
-      uint4 p = ld_stream(d), q = ld_stream(d + 4);
-      a.ctx[0] = p.x; a.ctx[1] = p.y; a.ctx[2] = p.z; a.ctx[3] = p.w;
-      a.ctx[4] = q.x; a.ctx[5] = q.y; a.ctx[6] = q.z; a.ctx[7] = q.w;
+    if (rc.nd.ctx) {
+      const int32_t* d = P.context_counts + slot * P.counts_stride + col[0];
+      const uint4 p = ld_stream(d), q = ld_stream(d + 4);
+      r.c[0] = p.x; r.c[1] = p.y; r.c[2] = p.z; r.c[3] = p.w;
+      r.c[4] = q.x; r.c[5] = q.y; r.c[6] = q.z; r.c[7] = q.w;
     }
-    if (n.bias) {
-      uint4 q = ld_stream(P.bias + slot * P.bias_stride + c);
-      const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        a.bias[2 * i] = __uint_as_float(w[i] << 16);
-        a.bias[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
-      }
+    if (rc.nd.bias) {
+      const uint4 q = ld_stream(P.bias + slot * P.bias_stride + col[0]);
+      r.b[0] = q.x; r.b[1] = q.y; r.b[2] = q.z; r.b[3] = q.w;
     }
   } else {
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const bool ok = j < nvalid;
-      const int64_t c = cc.col[j];
-      a.dec[j] = (n.dec && ok) ? __ldcs(P.decode_counts + slot * P.counts_stride + c) : 0;
-      a.ctx[j] = (n.ctx && ok) ? __ldcs(P.context_counts + slot * P.counts_stride + c) : 0;
-      a.bias[j] = (n.bias && ok) ? bf2f(__ldcs(P.bias + slot * P.bias_stride + c)) : 0.0f;
+      r.d[j] = (rc.nd.dec && ok) ? __ldcs(P.decode_counts + slot * P.counts_stride + col[j]) : 0;
+      r.c[j] = (rc.nd.ctx && ok) ? __ldcs(P.context_counts + slot * P.counts_stride + col[j]) : 0;
+    }
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const bool lo_ok = rc.nd.bias && 2 * p < nvalid, hi_ok = rc.nd.bias && 2 * p + 1 < nvalid;
+      const uint32_t lo = lo_ok ? (uint32_t)__ldcs(P.bias + slot * P.bias_stride + col[2 * p]) : 0u;
+      const uint32_t hi = hi_ok ? (uint32_t)__ldcs(P.bias + slot * P.bias_stride + col[2 * p + 1]) : 0u;
+      r.b[p] = lo | (hi << 16);
     }
   }
 }
 
-template <bool VEC>
-__device__ __forceinline__ uint32_t load_gbits8(const SonicSamplingParams& P, int64_t grow,
-                                                const Cols8& cc, int nvalid) {
+template <int MODE>
+__device__ __forceinline__ uint32_t load_g8(const SonicSamplingParams& P, int64_t grow, const int64_t (&col)[VPT],
+                                            int nvalid) {
   const uint32_t* g = P.grammar + grow * P.grammar_stride;
-  if (VEC && nvalid == VPT) {
-    const int64_t c = cc.col[0];
-    return (__ldg(g + (c >> 5)) >> (c & 31)) & 0xffu;
-  }
+  if (MODE != kScalar && nvalid == VPT) return (__ldg(g + (col[0] >> 5)) >> (col[0] & 31)) & 0xffu;
   uint32_t bits = 0;
 #pragma unroll
   for (int j = 0; j < VPT; ++j)
-    if (j < nvalid) bits |= ((__ldg(g + (cc.col[j] >> 5)) >> (cc.col[j] & 31)) & 1u) << j;
+    if (j < nvalid) bits |= ((__ldg(g + (col[j] >> 5)) >> (col[j] & 31)) & 1u) << j;
   return bits;
 }
 
@@ -265,19 +383,19 @@ __device__ __forceinline__ uint32_t load_gbits8(const SonicSamplingParams& P, in
 // shared-memory candidate buffer
 // ---------------------------------------------------------------------------------------
 
-// Append the keys of the set bits of `m` (block-wide call, warp-aggregated atomics).
+// Append the keys of the set bits of `m` (warp-aggregated atomics). Returns, on every lane,
+// the buffer count right after this warp's append (0 when the warp appended nothing).
 template <typename K>
-__device__ __forceinline__ void cand_push(K* buf, int* cnt, const K (&key)[VPT], unsigned m,
-                                          int lane) {
+__device__ __forceinline__ int cand_push(K* buf, int* cnt, const K (&key)[VPT], unsigned m, int lane) {
   const int np = __popc(m);
   int incl = np;
 #pragma unroll
   for (int d = 1; d < 32; d <<= 1) {
-    int y = __shfl_up_sync(kFull, incl, d);
+    const int y = __shfl_up_sync(kFull, incl, d);
     if (lane >= d) incl += y;
   }
   const int total = __shfl_sync(kFull, incl, 31);
-  if (total == 0) return;
+  if (total == 0) return 0;
   int base = 0;
   if (lane == 31) base = atomicAdd(cnt, total);
   base = __shfl_sync(kFull, base, 31);
@@ -285,6 +403,7 @@ __device__ __forceinline__ void cand_push(K* buf, int* cnt, const K (&key)[VPT],
 #pragma unroll
   for (int j = 0; j < VPT; ++j)
     if ((m >> j) & 1u) buf[pos++] = key[j];
+  return base + total;
 }
 
 template <typename K>
@@ -339,21 +458,10 @@ __device__ __forceinline__ uint64_t to_global<uint64_t>(uint64_t k, int64_t c0) 
   return (k & 0xffffffff00000000ull) | (uint64_t)(0xffffffffu - (uint32_t)col);
 }
 
-template <typename K>
-__device__ __forceinline__ K make_key(float v, int local);
-template <>
-__device__ __forceinline__ uint32_t make_key<uint32_t>(float v, int local) {
-  return (enc16(f2bf(v)) << 16) | (uint32_t)(0xffff - local);
-}
-template <>
-__device__ __forceinline__ uint64_t make_key<uint64_t>(float v, int local) {
-  return ((uint64_t)enc32(v) << 32) | (uint64_t)(0xffffffffu - (uint32_t)local);
-}
-
 // Final per-split step: exact top-128 of the buffer, sorted, written as global keys.
 template <typename K>
-__device__ void split_finish(K* buf, int* cnt, float* thr, K* top, int* tcnt, int* hist, int* bcast,
-                             int64_t c0, uint64_t* out) {
+__device__ void split_finish(K* buf, int* cnt, float* thr, K* top, int* tcnt, int* hist, int* bcast, int64_t c0,
+                             uint64_t* out) {
   __syncthreads();
   if (*cnt > kMaxK) cand_compact<K>(buf, cnt, thr, top, tcnt, hist, bcast);
   const int n = *cnt;
@@ -367,7 +475,7 @@ __device__ void split_finish(K* buf, int* cnt, float* thr, K* top, int* tcnt, in
     }
     warp_sort128_desc(k, lane);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) __stcg(reinterpret_cast<unsigned long long*>(out + 4 * lane + j), (unsigned long long)k[j]);
+    for (int j = 0; j < 4; ++j) stcg64(out + 4 * lane + j, k[j]);
     __threadfence();
   }
 }
@@ -389,8 +497,7 @@ __device__ __forceinline__ bool arrive_last(uint32_t* ticket, int splits, int* f
 }
 
 // Fold `splits` sorted candidate lists (u64 keys, descending) into one (warp-wide).
-__device__ __forceinline__ void warp_fold_lists(const uint64_t* lists, int splits, int lane,
-                                                uint64_t (&acc)[4]) {
+__device__ __forceinline__ void warp_fold_lists(const uint64_t* lists, int splits, int lane, uint64_t (&acc)[4]) {
 #pragma unroll
   for (int j = 0; j < 4; ++j) acc[j] = ldcg64(lists + 4 * lane + j);
   for (int s = 1; s < splits; ++s) {
@@ -409,29 +516,48 @@ __device__ __forceinline__ void decode_keys(const uint64_t (&k)[4], float (&v)[4
   }
 }
 
+// Per-slot masking parameters, loaded early so the selection epilogue does not wait on them.
+struct MaskParams {
+  int32_t top_k, top_logprobs;
+  uint16_t top_p, min_p;
+  bool has_k, has_p, has_min_p;
+};
+
+__device__ __forceinline__ MaskParams load_mask_params(const SonicSamplingParams& P, int64_t slot) {
+  MaskParams m;
+  m.has_k = P.top_k != nullptr;
+  m.has_p = P.top_p != nullptr;
+  m.has_min_p = P.min_p != nullptr;
+  m.top_k = m.has_k ? P.top_k[slot] : 0;
+  m.top_p = m.has_p ? P.top_p[slot] : 0;
+  m.min_p = m.has_min_p ? P.min_p[slot] : 0;
+  m.top_logprobs = P.top_logprobs ? P.top_logprobs[slot] : 0;
+  return m;
+}
+
 // cumulative_masking (ops/base.py:95-129) on the sorted top-128 held 4 per lane.
-__device__ __forceinline__ void warp_masking(const SonicSamplingParams& P, int64_t slot, uint32_t ind,
-                                             float (&v)[4], float maximum, int lane) {
+__device__ __forceinline__ void warp_masking(const MaskParams& M, uint32_t ind, float (&v)[4], float maximum,
+                                             int lane) {
   const float ninf = __int_as_float(0xff800000);
-  if ((ind & 0x80) && P.top_k) {
-    const int32_t k = P.top_k[slot];
+  if ((ind & 0x80) && M.has_k) {
+    const int32_t k = M.top_k;
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (!(4 * lane + j < k)) v[j] = ninf;
   }
-  if ((ind & 0x100) && P.top_p) {
+  if ((ind & 0x100) && M.has_p) {
     float e[4], lad[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) e[j] = dexp(__fsub_rn(v[j], maximum));
     warp_ladder128(e, lad, lane);
     const float total = __shfl_sync(kFull, lad[3], 31);
-    const float scale = __fmul_rn(total, bf2f(P.top_p[slot]));
+    const float scale = __fmul_rn(total, bf2f(M.top_p));
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (!(lad[j] <= scale || (lane == 0 && j == 0))) v[j] = ninf;
   }
-  if ((ind & 0x200) && P.min_p) {
-    const float pivot = __fadd_rn(dlog(bf2f(P.min_p[slot])), maximum);
+  if ((ind & 0x200) && M.has_min_p) {
+    const float pivot = __fadd_rn(dlog(bf2f(M.min_p)), maximum);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (!(v[j] >= pivot)) v[j] = ninf;
@@ -451,44 +577,350 @@ __device__ __forceinline__ void warp_log_softmax(const float (&v)[4], float maxi
   for (int j = 0; j < 4; ++j) ls[j] = __fsub_rn(sc[j], lse);
 }
 
-__device__ __forceinline__ void store_float(void* base, int32_t dtype, int64_t i, float x) {
-  if (dtype == SONIC_DTYPE_F32)
-    ((float*)base)[i] = x;
-  else
-    ((uint16_t*)base)[i] = f2bf(x);
-}
-
-__device__ __forceinline__ int64_t load_slot(const SonicSamplingParams& P, int64_t unit) {
-  return P.slot_mapping ? load_index(P.slot_mapping, P.slot_dtype, unit) : unit;
-}
+constexpr float kFiniteFloor = -3.40282346638528859811704183484516925e+38f;  // -FLT_MAX
 
 // ---------------------------------------------------------------------------------------
-// shared memory of a single-row CTA
+// per-warp streaming top-128 of the single-row kernels
 // ---------------------------------------------------------------------------------------
+//
+// Each warp keeps the 128 largest keys it has seen, sorted, in registers (4 per lane), plus a
+// shared-memory queue of new keys at or above the CTA's cut. When 128 or more keys are
+// queued the warp sorts them in blocks of 128 and merges each block into its list: no
+// block-wide synchronisation. The cut is the largest 128th-kept-key value of any warp (128
+// keys of the split are at least that large, so nothing below it can be in the split's
+// top-128); it lives in shared memory as (enc32(value) << 32) | fast-path pre-temperature
+// pair, both monotone in the value, so one 64-bit atomicMax publishes it. At the end of a
+// split warp 0 merges the 8 lists.
+
+constexpr int NW = NT / 32;
+constexpr int QCAP = kMaxK + VPT * 32;  // a warp appends at most 256 keys per chunk
 
 template <typename K>
-struct RowSmem {
-  K buf[CAP];
-  K top[kMaxK];
-  int hist[256];
-  int bcast[4];
-  int cnt;
-  int tcnt;
-  int flag;
-  float thr;
-  uint64_t warp_best[NT / 32];
-  int32_t toks[SONIC_MAX_LOOKAHEAD + 1];
+struct WarpTopK {
+  K* list;         // shared memory, 128 keys sorted descending
+  int qn;          // queued keys (warp-uniform)
+  float thr;       // candidate threshold, final-value domain (warp-uniform)
+  uint32_t vmin2;  // fast path: pre-temperature threshold pair (warp-uniform)
+  unsigned long long cut;  // packed (thr, vmin2), see pack_cut
 };
+
+__device__ __forceinline__ unsigned long long pack_cut(float thr, uint32_t vmin2) {
+  return ((unsigned long long)enc32(thr) << 32) | vmin2;
+}
+
+template <typename K>
+__device__ __forceinline__ void wtk_init(WarpTopK<K>& w, K* list, float thr0, int lane) {
+  w.list = list;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) list[4 * lane + j] = 0;
+  __syncwarp();
+  w.qn = 0;
+  w.thr = thr0;
+  w.vmin2 = 0;
+  w.cut = pack_cut(thr0, 0);
+}
+
+// take the CTA's cut when another warp raised it
+template <typename K>
+__device__ __forceinline__ void wtk_adopt(WarpTopK<K>& w, const unsigned long long* cut, int lane) {
+  unsigned long long c = 0;
+  if (lane == 0) c = *reinterpret_cast<const volatile unsigned long long*>(cut);
+  c = __shfl_sync(kFull, c, 0);
+  if (c > w.cut) {
+    w.cut = c;
+    w.thr = dec32((uint32_t)(c >> 32));
+    w.vmin2 = (uint32_t)c;
+  }
+}
+
+// raise this warp's threshold to `t` (with its fast-path pair `vm`) and publish it
+template <typename K>
+__device__ __forceinline__ void wtk_raise(WarpTopK<K>& w, unsigned long long* cut, float t, uint32_t vm, int lane) {
+  w.thr = t;
+  w.vmin2 = vm;
+  w.cut = pack_cut(t, vm);
+  if (lane == 0) atomicMax(cut, w.cut);
+}
+
+// warp-exclusive offsets of `np` items per lane; returns the warp total
+__device__ __forceinline__ int warp_offsets(int np, int lane, int& excl) {
+  int incl = np;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int y = __shfl_up_sync(kFull, incl, d);
+    if (lane >= d) incl += y;
+  }
+  excl = incl - np;
+  return __shfl_sync(kFull, incl, 31);
+}
+
+// append the keys of the set bits of `m` to the warp queue
+template <typename K>
+__device__ __forceinline__ void wtk_push(WarpTopK<K>& w, K* q, const K (&key)[VPT], unsigned m, int lane) {
+  if (!__any_sync(kFull, m)) return;
+  int excl;
+  const int total = warp_offsets(__popc(m), lane, excl);
+  int pos = w.qn + excl;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j)
+    if ((m >> j) & 1u) q[pos++] = key[j];
+  w.qn += total;
+}
+
+// Sort the `qn` queued keys in blocks of 128 and merge each block into the warp's sorted
+// list (both in shared memory); returns the value of the 128th kept key (-inf while fewer
+// than 128 are kept). Not inlined: it runs rarely and is large, and one copy keeps the
+// streaming loop inside the instruction cache.
+template <typename K>
+__device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane) {
+  __syncwarp();
+  K l[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) l[j] = list[4 * lane + j];
+  for (int base = 0; base < qn; base += kMaxK) {
+    K k[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = base + 4 * lane + j;
+      k[j] = i < qn ? q[i] : (K)0;
+    }
+    warp_sort128_desc(k, lane);
+    warp_merge128_desc(l, k, lane);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) list[4 * lane + j] = l[j];
+  __syncwarp();
+  const K last = __shfl_sync(kFull, l[3], 31);
+  return last != 0 ? key_value<K>(last) : __int_as_float(0xff800000);
+}
+
+template <typename K>
+__device__ __forceinline__ float wtk_absorb(WarpTopK<K>& w, const K* q, int lane) {
+  const float t = absorb_queue<K>(w.list, q, w.qn, lane);
+  w.qn = 0;
+  return t;
+}
+
+// Merge the NW warp lists (shared memory, overwritten) into warp 0's registers with a
+// 3-round tree. Block-wide.
+template <typename K>
+__device__ void block_fold(K (*lists)[kMaxK], int warp, int lane, K (&out)[4]) {
+  __syncthreads();
+#pragma unroll
+  for (int width = NW / 2; width >= 1; width >>= 1) {
+    if (warp < width) {
+      K b[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        out[j] = lists[warp][4 * lane + j];
+        b[j] = lists[warp + width][4 * lane + j];
+      }
+      warp_merge128_desc(out, b, lane);
+      if (width > 1)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) lists[warp][4 * lane + j] = out[j];
+    }
+    __syncthreads();
+  }
+}
+
+__device__ __forceinline__ int64_t key_column(uint64_t g) { return (int64_t)(0xffffffffu - (uint32_t)g); }
+
+// Merge `splits` sorted candidate lists of 128 u64 keys (workspace) into warp 0's registers.
+// Warp v folds lists v, v+8, ... (all its loads issued at once), then a 3-round tree over
+// shared memory (`xchg`, NW x 128 u64) combines the warp results. Block-wide.
+__device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* xchg, int warp, int lane,
+                                  uint64_t (&out)[4]) {
+  uint64_t acc[4] = {0, 0, 0, 0};
+  if (warp < splits) {
+    constexpr int PER = MAX_SPLITS / NW;
+    uint64_t pre[PER][4];
+#pragma unroll
+    for (int t = 0; t < PER; ++t) {
+      const int s = warp + t * NW;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pre[t][j] = s < splits ? ldcg64(lists + (int64_t)s * kMaxK + 4 * lane + j) : 0ull;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] = pre[0][j];
+#pragma unroll
+    for (int t = 1; t < PER; ++t)
+      if (warp + t * NW < splits) warp_merge128_desc(acc, pre[t], lane);
+  }
+  for (int width = NW / 2; width >= 1; width >>= 1) {
+    if (warp >= width && warp < 2 * width)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) xchg[(warp - width) * kMaxK + 4 * lane + j] = acc[j];
+    __syncthreads();
+    if (warp < width) {
+      uint64_t b[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = xchg[warp * kMaxK + 4 * lane + j];
+      warp_merge128_desc(acc, b, lane);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) out[j] = acc[j];
+}
+
+// ---------------------------------------------------------------------------------------
+// single-row streaming: warp-private groups of 256 columns (8 per lane). Each warp owns a
+// ring of bulk-copy stages (one group each) that its lane 0 refills as soon as the warp
+// has consumed a stage, so several groups per warp are always in flight and warps never
+// wait for one another until the split's lists are folded. Groups the ring cannot take
+// (a ragged tail, unaligned or gathered rows) use direct loads.
+// ---------------------------------------------------------------------------------------
+
+constexpr int GROUP = VPT * 32;  // columns of one warp group
+constexpr int PF_GROUPS = 4;     // L2 prefetch distance of direct loads, in groups of one warp
+constexpr int WST = 3;           // bulk-copy stages per warp
+// stage layout (bytes) of one group: logits, decode counts, context counts, bias, grammar
+constexpr int WS_X = 0;
+constexpr int WS_D = WS_X + GROUP * 2;
+constexpr int WS_C = WS_D + GROUP * 4;
+constexpr int WS_B = WS_C + GROUP * 4;
+constexpr int WS_G = WS_B + GROUP * 2;
+constexpr int WS_BYTES = WS_G + GROUP / 8;  // 3104
+
+__device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Smallest bf16 v (finite or +inf, as a bf16 pair) whose final value is >= thr: a guess
+// from thr * temperature, corrected a few steps along the order-preserving encoding (the
+// final value is monotone in v); binary search when the guess is far off.
+__device__ __noinline__ uint32_t vmin_pair(float thr, bool on, bool fast, float t, float rt) {
+  constexpr uint32_t kLo = 0x0080u, kHi = 0xff80u;  // enc of -max finite .. enc of +inf
+  auto ok = [&](uint32_t e) { return temper(bf2f((uint16_t)dec16(e)), on, fast, t, rt) >= thr; };
+  const float guess = on ? __fmul_rn(thr, t) : thr;
+  uint32_t e = umin(umax(enc16(f2bf(guess)), kLo), kHi);
+  bool done = false;
+  if (ok(e)) {
+    for (int i = 0; i < 4 && !done; ++i) {
+      if (e == kLo || !ok(e - 1)) done = true;
+      else --e;
+    }
+  } else {
+    for (int i = 0; i < 4 && !done; ++i) {
+      if (e == kHi) break;
+      ++e;
+      if (ok(e)) done = true;
+    }
+  }
+  if (!done) {
+    uint32_t lo = kLo, hi = kHi;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi) >> 1;
+      if (ok(mid)) hi = mid;
+      else lo = mid + 1;
+    }
+    e = lo;
+  }
+  const uint32_t h = dec16(e);
+  return h | (h << 16);
+}
+
+__device__ __forceinline__ uint32_t vmin_pair(float thr, const RowConsts& rc) {
+  return vmin_pair(thr, rc.nd.temp, rc.temp_fast, rc.temp, rc.rtemp);
+}
+
+// Shared-memory state of a single-row CTA.
+template <typename K>
+struct RowSmem {
+  K queue[NW][QCAP];
+  K lists[NW][kMaxK];
+  unsigned long long cut;  // packed CTA cut, see pack_cut
+  float v16[NW];           // each warp's 16th kept key value (-inf while it keeps fewer)
+  float vlm[NW];           // each warp's 16th largest lane maximum (see lane_max_cut)
+  MaskParams mp;           // the slot's masking parameters (selection epilogue)
+  int flag;
+  unsigned long long best;
+  int32_t toks[SONIC_MAX_LOOKAHEAD + 1];
+  uint64_t bars[NW][WST];
+};
+
+// After an absorb: the warp's new threshold candidates are its own 128th key value and the
+// smallest 16th key value over all warps (the 8 top-16 sets are 128 distinct keys).
+template <typename K>
+__device__ __forceinline__ float absorbed_cut(const WarpTopK<K>& w, float own128, float* v16, int warp, int lane) {
+  const K k16 = w.list[15];
+  if (lane == 0) reinterpret_cast<volatile float*>(v16)[warp] = k16 ? key_value<K>(k16) : __int_as_float(0xff800000);
+  __syncwarp();
+  float m = lane < NW ? reinterpret_cast<volatile float*>(v16)[lane] : __int_as_float(0x7f800000);
+#pragma unroll
+  for (int d = 4; d >= 1; d >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, d));
+  m = __shfl_sync(kFull, m, 0);
+  return fmaxf(own128, m);
+}
+
+// descending bitonic sort of one value per lane
+__device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v, int lane) {
+#pragma unroll
+  for (int size = 2; size <= 32; size <<= 1) {
+#pragma unroll
+    for (int d = size >> 1; d >= 1; d >>= 1) {
+      const uint32_t o = __shfl_xor_sync(kFull, v, d);
+      const bool keep_max = ((lane & d) == 0) == ((lane & size) == 0 || size == 32);
+      v = keep_max ? umax(v, o) : umin(v, o);
+    }
+  }
+  return v;
+}
+
+// Each lane's largest pushed key belongs to a distinct column, so the 16th largest lane
+// maximum of every warp bounds 8 x 16 = 128 distinct keys of the split from below: the
+// smallest of those over the warps is a valid cut. Warp-wide; returns that cut (-inf while
+// some warp has not published).
+__device__ __forceinline__ float lane_max_cut(uint32_t lmax, float* vlm, int warp, int lane) {
+  const uint32_t k16 = __shfl_sync(kFull, warp_sort32_desc(lmax, lane), 15);
+  if (lane == 0) reinterpret_cast<volatile float*>(vlm)[warp] = k16 ? key_value<uint32_t>(k16) : __int_as_float(0xff800000);
+  __syncwarp();
+  float m = lane < NW ? reinterpret_cast<volatile float*>(vlm)[lane] : __int_as_float(0x7f800000);
+#pragma unroll
+  for (int d = 4; d >= 1; d >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, d));
+  return __shfl_sync(kFull, m, 0);
+}
+
+__device__ __forceinline__ uint32_t select4(const uint32_t (&v)[4], int i) {
+  return i < 2 ? (i == 0 ? v[0] : v[1]) : (i == 2 ? v[2] : v[3]);
+}
+
+template <typename K>
+__device__ __forceinline__ void row_smem_init(RowSmem<K>& st, unsigned long long cut0) {
+  st.cut = cut0;
+  for (int i = 0; i < NW; ++i) st.v16[i] = st.vlm[i] = __int_as_float(0xff800000);
+}
+
+// Loads of one group of 8 columns per lane (`c` = first column of this lane).
+template <int MODE, bool INDIRECT>
+__device__ __forceinline__ void load_group(const SonicSingularArgs& a, const RowConsts& rc, int64_t slot,
+                                           const uint16_t* xrow, int64_t c, int nvalid, Raw8& raw) {
+  constexpr int AM = INDIRECT ? kScalar : MODE;
+  load_x8<MODE>(xrow, c, nvalid, raw.x);
+  raw.g = 0xffu;
+  if (rc.nd.proc) {
+    int64_t col[VPT];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      col[j] = c + j + a.shard_offset;
+      if (INDIRECT && j < nvalid) col[j] = load_index(a.d2t, a.d2t_dtype, col[j]);
+    }
+    load_aux8<AM>(a.params, rc, slot, col, nvalid, raw);
+    if (rc.nd.g) raw.g = load_g8<AM>(a.params, slot, col, nvalid);
+  }
+}
 
 // ---------------------------------------------------------------------------------------
 // fused singular: prologue + top-128 per split + merge + selection
 // (ops/prologue.py:272 + ops/singular.py:154)
 // ---------------------------------------------------------------------------------------
 
-template <bool VEC, bool INDIRECT>
-__global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols,
-                                                      int log2bn, uint64_t* cand, uint32_t* tickets) {
-  __shared__ RowSmem<uint32_t> sm;
+template <int MODE, bool INDIRECT>
+__global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
+                                                      Workspace ws) {
+  __shared__ __align__(16) RowSmem<uint32_t> st;
+  extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
   const int64_t r = blockIdx.y;
@@ -505,88 +937,295 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     return;
   }
   const uint32_t ind = P.indicators[slot];
-  const Needs nd = row_needs(P, ind);
-  const RowParams rp = load_row_params(P, slot, ind);
+  const RowConsts rc = row_consts(P, slot, ind);
   const bool greedy = (ind & 0x40) != 0;
-  const int ntok = (a.drafted_tokens && nd.dec) ? a.lookahead : 0;
-  if (tid < ntok) sm.toks[tid] = a.drafted_tokens[slot * a.drafted_stride + tid];
+  const int ntok = (a.drafted_tokens && rc.nd.dec) ? a.lookahead : 0;
+  if (tid < ntok) st.toks[tid] = a.drafted_tokens[slot * a.drafted_stride + tid];
   if (tid == 0) {
-    sm.cnt = 0;
-    sm.thr = __int_as_float(0xff800000);
+    st.best = 0ull;
+    st.mp = load_mask_params(P, slot);
+    row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
   }
   __syncthreads();
 
   const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
+  const int64_t shard = a.shard_offset;
+  uint32_t* q = st.queue[warp];
+  WarpTopK<uint32_t> w;
+  wtk_init(w, st.lists[warp], kFiniteFloor, lane);  // the first wtk_adopt takes the fast-path pair from st.cut
   uint64_t best = 0;
+  uint32_t lmax = 0;  // largest key this lane has pushed (fast path)
 
-#pragma unroll 1
-  for (int64_t cb = c0; cb < c1; cb += CHUNK) {
-    const int64_t c = cb + (int64_t)VPT * tid;
-    const int nvalid = (int)max((int64_t)0, min((int64_t)VPT, c1 - c));
-    float x[VPT];
-    load_logits8<VEC>(xrow, c, nvalid, x);
-    if (nd.proc || nd.temp) {
-      Cols8 cc;
+  auto absorb_if_full = [&]() {
+    if (w.qn >= kMaxK) {
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane), st.v16, warp, lane);
+      if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
+    }
+  };
+
+  // exact path: every processor on every column, then the candidate test
+  auto exact_group = [&](Raw8& raw, int64_t c, int nvalid) {
+    if (rc.nd.proc && ntok) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        int64_t col = c + j + a.shard_offset;
-        if (INDIRECT && nd.proc && j < nvalid) col = load_index(a.d2t, a.d2t_dtype, col);
-        cc.col[j] = col;
-      }
-      Aux8 ax;
-      load_aux8<VEC && !INDIRECT>(P, nd, slot, cc, nvalid, ax);
-      const uint32_t gb = nd.g ? load_gbits8<VEC && !INDIRECT>(P, slot, cc, nvalid) : 0xffu;
-#pragma unroll
-      for (int j = 0; j < VPT; ++j) {
-        int32_t dec = ax.dec[j];
-        for (int s = 0; s < ntok; ++s) dec += (sm.toks[s] == cc.col[j]);
-        x[j] = apply_processors(x[j], ind, nd, (gb >> j) & 1u, dec, ax.ctx[j], ax.bias[j], rp);
+        const int64_t col = INDIRECT ? -1 : c + j + shard;
+        for (int s = 0; s < ntok; ++s) raw.d[j] += (st.toks[s] == col);
       }
     }
+    if (rc.nd.proc || rc.nd.temp) process8(raw, rc);
     if (greedy) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j)
-        if (j < nvalid) best = umax(best, greedy_key(x[j], c + j, log2bn));
-    } else {
-      const float thr = sm.thr;
-      uint32_t key[VPT];
-      unsigned m = 0;
+        if (j < nvalid) best = umax(best, greedy_key_bits(half_of(raw.x, j), c + j, log2bn));
+      return;
+    }
+    const float thr = w.thr;
+    uint32_t key[VPT];
+    unsigned m = 0;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const uint32_t h = half_of(raw.x, j);
+      key[j] = (enc16(h) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
+      if (j < nvalid && bf2f((uint16_t)h) >= thr) m |= 1u << j;
+    }
+    wtk_push(w, q, key, m, lane);
+  };
+
+  // fast path (see vmin_pair): temperature only for candidates, grammar as a mask bit, and
+  // penalties only where a count is nonzero (they are the identity elsewhere). Where the
+  // penalties cannot raise a logit (rc.decr, counts >= 0) the candidate test runs on the
+  // unpenalised value first and only candidates are penalised and tested again.
+  auto fast_group = [&](const Raw8& raw, int64_t c, int nvalid) {
+    uint32_t x[4] = {raw.x[0], raw.x[1], raw.x[2], raw.x[3]};
+    // columns whose counts (or drafted tokens) are nonzero; computed only when needed
+    auto need_bits = [&]() {
+      uint32_t need = 0;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) need |= (uint32_t)((raw.d[j] | (rc.nd.ctx ? raw.c[j] : 0)) != 0) << j;
+      for (int t = 0; t < ntok; ++t) {
+        const int64_t dl = (int64_t)st.toks[t] - (c + shard);
+        if (dl >= 0 && dl < nvalid) need |= 1u << dl;
+      }
+      return need;
+    };
+    auto penalise = [&](uint32_t (&v)[4], uint32_t bits) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        key[j] = make_key<uint32_t>(x[j], (int)(c + j - c0));
-        if (j < nvalid && x[j] >= thr) m |= 1u << j;
+        if ((bits >> j) & 1u) {
+          int32_t dj = raw.d[j];
+          for (int t = 0; t < ntok; ++t) dj += (st.toks[t] == c + j + shard);
+          const uint32_t h = repetition_one(half_of(v, j), dj, rc.nd.ctx ? raw.c[j] : 0, rc);
+          v[j >> 1] = (j & 1) ? ((v[j >> 1] & 0xffffu) | (h << 16)) : ((v[j >> 1] & 0xffff0000u) | h);
+        }
       }
-      cand_push<uint32_t>(sm.buf, &sm.cnt, key, m, lane);
-      __syncthreads();
-      const bool full = sm.cnt > CAP - CHUNK;
-      __syncthreads();
-      if (full) cand_compact<uint32_t>(sm.buf, &sm.cnt, &sm.thr, sm.top, &sm.tcnt, sm.hist, sm.bcast);
+    };
+    bool counted = ntok > 0;  // some count of this lane's columns may be nonzero
+    if (rc.nd.dec) {
+      int32_t any = 0;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) any |= raw.d[j] | (rc.nd.ctx ? raw.c[j] : 0);
+      counted = counted || any != 0;
+      // penalties that may raise a logit go in before the candidate test
+      const bool before = counted && (!rc.decr || any < 0);
+      if (__any_sync(kFull, before)) {
+        if (before) penalise(x, need_bits());
+        counted = counted && !before;
+      }
+    }
+    uint32_t y[4] = {x[0], x[1], x[2], x[3]};
+    if (rc.nd.bias) {
+#pragma unroll
+      for (int p = 0; p < 4; ++p) y[p] = bf2_add(x[p], raw.b[p]);
+    }
+    uint32_t m = ge_mask8(y, w.vmin2) & raw.g;
+    if (nvalid < VPT) m &= (1u << max(nvalid, 0)) - 1u;
+    if (!__any_sync(kFull, m)) return;
+    // candidates of the unpenalised test: penalise those with nonzero counts, test again
+    if (__any_sync(kFull, counted && m)) {
+      const uint32_t late = (counted && m) ? (m & need_bits()) : 0u;
+      if (late) {
+        penalise(x, late);
+#pragma unroll
+        for (int p = 0; p < 4; ++p) y[p] = rc.nd.bias ? bf2_add(x[p], raw.b[p]) : x[p];
+        m &= ge_mask8(y, w.vmin2) | ~late;
+      }
+    }
+    int excl;
+    const int total = warp_offsets(__popc(m), lane, excl);
+    int pos = w.qn + excl;
+    const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      const uint32_t word = select4(y, j >> 1);
+      const float fv = final_value(bf2f((uint16_t)((j & 1) ? (word >> 16) : (word & 0xffffu))), rc);
+      const uint32_t key = (enc16(f2bf(fv)) << 16) | (base - (uint32_t)j);
+      q[pos++] = key;
+      lmax = umax(lmax, key);
+    }
+    w.qn += total;
+  };
+
+  auto process_group = [&](Raw8& raw, int64_t c, int nvalid, int k) {
+    if (!greedy) wtk_adopt(w, &st.cut, lane);
+    if (rc.fast) {
+      fast_group(raw, c, nvalid);
+      if (k < 3) {
+        // bootstrap the cut from the lane maxima of the first groups
+        const float t = lane_max_cut(lmax, st.vlm, warp, lane);
+        if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
+      }
+    } else {
+      exact_group(raw, c, nvalid);
+    }
+    if (!greedy) absorb_if_full();
+  };
+
+  // groups of this warp: g = warp, warp + NW, ...; columns [c0 + g * GROUP, +GROUP)
+  const int ngroups = (int)((c1 - c0 + GROUP - 1) / GROUP);
+  auto gcol = [&](int g) { return c0 + (int64_t)g * GROUP + (int64_t)VPT * lane; };
+  auto gvalid = [&](int g) { return (int)max((int64_t)0, min((int64_t)VPT, c1 - gcol(g))); };
+  constexpr int DM = MODE == kTma ? kVec : MODE;  // direct loads
+
+  // full groups go through this warp's bulk-copy ring: its k-th group uses stage k % WST
+  const int nfull = MODE == kTma ? (int)((c1 - c0) / GROUP) : 0;
+  const int kfull = nfull > warp ? (nfull - warp + NW - 1) / NW : 0;
+  unsigned char* ring = smem_ring + (size_t)warp * WST * WS_BYTES;
+  const uint32_t* grow = rc.nd.g ? P.grammar + slot * P.grammar_stride : nullptr;
+  const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
+  const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
+  const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
+  const uint32_t tx =
+      GROUP * 2 + (drow ? GROUP * 4 : 0) + (crow ? GROUP * 4 : 0) + (brow ? GROUP * 2 : 0) + (grow ? GROUP / 8 : 0);
+  // lane i < 5 issues stream i (logits, decode counts, context counts, bias, grammar)
+  const unsigned char* sbase = nullptr;
+  int64_t sadd = 0;
+  int ssh = 0, sdsh = 0, soff = 0;
+  uint32_t sbytes = 0;
+  if (lane == 0) { sbase = (const unsigned char*)xrow; ssh = 1; soff = WS_X; sbytes = GROUP * 2; }
+  if (lane == 1 && drow) { sbase = (const unsigned char*)drow; sadd = shard; ssh = 2; soff = WS_D; sbytes = GROUP * 4; }
+  if (lane == 2 && crow) { sbase = (const unsigned char*)crow; sadd = shard; ssh = 2; soff = WS_C; sbytes = GROUP * 4; }
+  if (lane == 3 && brow) { sbase = (const unsigned char*)brow; sadd = shard; ssh = 1; soff = WS_B; sbytes = GROUP * 2; }
+  if (lane == 4 && grow) { sbase = (const unsigned char*)grow; sadd = shard; sdsh = 3; soff = WS_G; sbytes = GROUP / 8; }
+  auto issue = [&](int k) {  // warp-wide
+    uint64_t* bar = &st.bars[warp][k % WST];
+    if (lane == 0) mbar_expect_tx(bar, tx);
+    __syncwarp();
+    if (sbase) {
+      const int64_t cc = c0 + (int64_t)(warp + k * NW) * GROUP + sadd;
+      bulk_load(ring + (k % WST) * WS_BYTES + soff, sbase + ((cc << ssh) >> sdsh), sbytes, bar);
+    }
+  };
+  if (kfull > 0) {
+    if (lane == 0) {
+      for (int i = 0; i < WST; ++i) mbar_init(&st.bars[warp][i], 1);
+      mbar_fence_init();
+    }
+    __syncwarp();
+    for (int k = 0; k < min(kfull, WST); ++k) issue(k);
+  }
+
+  bool werr = false;
+  for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
+    const int64_t c = gcol(g);
+    const int nv = gvalid(g);
+    Raw8 raw;
+    const bool staged = k < kfull;
+    if (staged) {
+      if (!mbar_wait_bounded(&st.bars[warp][k % WST], (uint32_t)(k / WST) & 1u, WAIT_LIMIT)) werr = true;
+      const unsigned char* sp = ring + (k % WST) * WS_BYTES;
+      const uint4 xq = *reinterpret_cast<const uint4*>(sp + WS_X + lane * 16);
+      raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) raw.d[j] = raw.c[j] = 0;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) raw.b[p] = 0;
+      raw.g = 0xffu;
+      if (drow) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_D + lane * 32);
+        const uint4 v = *reinterpret_cast<const uint4*>(sp + WS_D + lane * 32 + 16);
+        raw.d[0] = u.x; raw.d[1] = u.y; raw.d[2] = u.z; raw.d[3] = u.w;
+        raw.d[4] = v.x; raw.d[5] = v.y; raw.d[6] = v.z; raw.d[7] = v.w;
+      }
+      if (crow) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_C + lane * 32);
+        const uint4 v = *reinterpret_cast<const uint4*>(sp + WS_C + lane * 32 + 16);
+        raw.c[0] = u.x; raw.c[1] = u.y; raw.c[2] = u.z; raw.c[3] = u.w;
+        raw.c[4] = v.x; raw.c[5] = v.y; raw.c[6] = v.z; raw.c[7] = v.w;
+      }
+      if (brow) {
+        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_B + lane * 16);
+        raw.b[0] = u.x; raw.b[1] = u.y; raw.b[2] = u.z; raw.b[3] = u.w;
+      }
+      if (grow) raw.g = sp[WS_G + lane];
+    } else {
+      load_group<DM, INDIRECT>(a, rc, slot, xrow, c, nv, raw);
+    }
+    process_group(raw, c, nv, k);
+    if (staged) {
+      // every lane has consumed its loads of this stage: refill it
+      __syncwarp();
+      if (k + WST < kfull) issue(k + WST);
     }
   }
+  if (werr) atomicOr(ws.error, 1u);
   pdl_trigger();
 
-  uint64_t* lists = cand + (uint64_t)r * splits * kMaxK;
+  uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   if (greedy) {
     best = warp_max_u64(best);
-    if (lane == 0) sm.warp_best[warp] = best;
+    if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
     __syncthreads();
     if (tid == 0) {
-      uint64_t b = sm.warp_best[0];
-      for (int w = 1; w < NT / 32; ++w) b = umax(b, sm.warp_best[w]);
-      __stcg(reinterpret_cast<unsigned long long*>(lists + (int64_t)split * kMaxK), (unsigned long long)b);
+      stcg64(lists + (int64_t)split * kMaxK, st.best);
       __threadfence();
     }
   } else {
-    split_finish<uint32_t>(sm.buf, &sm.cnt, &sm.thr, sm.top, &sm.tcnt, sm.hist, sm.bcast, c0,
-                           lists + (int64_t)split * kMaxK);
+    if (w.qn) wtk_absorb(w, q, lane);
+    uint32_t fin[4];
+    block_fold(st.lists, warp, lane, fin);
+    if (warp == 0) {
+      const uint32_t last = __shfl_sync(kFull, fin[3], 31);
+      if (lane == 0) st.flag = last != 0;
+    }
+    __syncthreads();
+    if (!st.flag) {
+      // fewer than 128 finite candidates in this split: redo it keeping -inf logits,
+      // through the exact path
+      if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
+      __syncthreads();
+      wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
+      for (int gg = warp; gg < ngroups; gg += NW) {
+        Raw8 raw;
+        load_group<DM, INDIRECT>(a, rc, slot, xrow, gcol(gg), gvalid(gg), raw);
+        wtk_adopt(w, &st.cut, lane);
+        exact_group(raw, gcol(gg), gvalid(gg));
+        absorb_if_full();
+      }
+      if (w.qn) wtk_absorb(w, q, lane);
+      block_fold(st.lists, warp, lane, fin);
+    }
+    if (warp == 0) {
+      uint64_t* out = lists + (int64_t)split * kMaxK;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t key = to_global<uint32_t>(fin[j], c0);
+        stcg64(out + 4 * lane + j, key);
+        // warm L2 with the noise the merge will gather for this candidate
+        if (key && !(a.flags & SONIC_FLAG_PHILOX) && !a.d2t &&
+            (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
+      }
+      __threadfence();
+    }
   }
 
-  if (!arrive_last(tickets + r, splits, &sm.flag)) return;
-  if (warp != 0) return;
+  if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
 
-  // ---- merge + selection (one warp) ----
+  // ---- merge + selection ----
   const uint32_t flags = a.flags;
   if (greedy) {
+    if (warp != 0) return;
     uint64_t b = 0;
     for (int s = lane; s < splits; s += 32) b = umax(b, ldcg64(lists + (int64_t)s * kMaxK));
     b = warp_max_u64(b);
@@ -603,15 +1242,24 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
 
   uint64_t k[4];
-  warp_fold_lists(lists, splits, lane, k);
+  block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
+  if (warp != 0) return;
   float v[4];
   int64_t idx[4];
   decode_keys(k, v, idx);
-  const float vmax = __shfl_sync(kFull, v[0], 0);
-  if (ind & 0x380) warp_masking(P, slot, ind, v, vmax, lane);
   int64_t tok[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) tok[j] = a.d2t ? load_index(a.d2t, a.d2t_dtype, idx[j]) : idx[j];
+  // noise loads first: their latency overlaps the masking
+  uint16_t noise[4] = {0, 0, 0, 0};
+  bool off[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    off[j] = a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab);
+    if (!(flags & SONIC_FLAG_PHILOX) && !off[j]) noise[j] = a.gumbel[slot * a.gumbel_stride + tok[j]];
+  }
+  const float vmax = __shfl_sync(kFull, v[0], 0);
+  if (ind & 0x380) warp_masking(st.mp, ind, v, vmax, lane);
   float diff[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -619,9 +1267,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       diff[j] = __fsub_rn(v[j], philox_log_exponential(a.philox_seed, a.philox_offset, (uint32_t)slot,
                                                         (uint32_t)tok[j]));
     else
-      diff[j] = (a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab))
-                    ? __int_as_float(0xff800000)
-                    : rbf(__fsub_rn(v[j], bf2f(a.gumbel[slot * a.gumbel_stride + tok[j]])));
+      diff[j] = off[j] ? __int_as_float(0xff800000) : rbf(__fsub_rn(v[j], bf2f(noise[j])));
   }
   const int sel = warp_argmax128(diff, lane);
   const int64_t token = warp_pick128(tok, sel);
@@ -636,7 +1282,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       const float lsel = warp_pick128(ls, sel);
       if (lane == 0) store_float(a.logprobs, a.logprobs_dtype, r * a.logprobs_stride, lsel);
       if (a.max_top_logprobs > 0 && (ind & 0x400) && a.top_logprob_values && P.top_logprobs) {
-        const int z = min(P.top_logprobs[slot], a.max_top_logprobs);
+        const int z = min(st.mp.top_logprobs, a.max_top_logprobs);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const int i = 4 * lane + j;
@@ -663,66 +1309,140 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 // bounded top-k (ops/topk/bitpack.py:99 + ops/topk/unpack.py:312)
 // ---------------------------------------------------------------------------------------
 
-template <bool VEC, bool F32>
-__global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int splits, int cols,
-                                                  uint64_t* cand, uint32_t* tickets) {
+template <bool F32, bool VEC>
+__device__ __forceinline__ void load_vals8(const unsigned char* xrow, int64_t c, int nvalid, float (&x)[VPT]) {
+  if (F32) {
+    const float* xr = (const float*)xrow;
+    if (VEC && nvalid == VPT) {
+      const uint4 p = ld_stream(xr + c), u = ld_stream(xr + c + 4);
+      x[0] = __uint_as_float(p.x); x[1] = __uint_as_float(p.y); x[2] = __uint_as_float(p.z);
+      x[3] = __uint_as_float(p.w); x[4] = __uint_as_float(u.x); x[5] = __uint_as_float(u.y);
+      x[6] = __uint_as_float(u.z); x[7] = __uint_as_float(u.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) x[j] = j < nvalid ? __ldcs(xr + c + j) : 0.0f;
+    }
+  } else {
+    uint32_t wv[4];
+    load_x8<VEC ? kVec : kScalar>((const uint16_t*)xrow, c, nvalid, wv);
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      x[2 * p] = bf2_lo(wv[p]);
+      x[2 * p + 1] = bf2_hi(wv[p]);
+    }
+  }
+}
+
+template <int MODE, bool F32>
+__global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int splits, int cols, Workspace ws) {
   using K = typename std::conditional<F32, uint64_t, uint32_t>::type;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  RowSmem<K>& sm = *reinterpret_cast<RowSmem<K>*>(smem_raw);
+  constexpr int EB = F32 ? 4 : 2;  // element bytes
+  constexpr bool VEC = MODE == kVec;
+  __shared__ __align__(16) RowSmem<K> st;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
   const int64_t r = blockIdx.y;
   const int64_t c0 = (int64_t)split * cols;
   const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
+  const unsigned char* xrow = (const unsigned char*)a.logits + r * a.logits_stride * EB;
 
   pdl_wait();
-  if (tid == 0) {
-    sm.cnt = 0;
-    sm.thr = __int_as_float(0xff800000);
-  }
+  if (tid == 0) row_smem_init(st, pack_cut(kFiniteFloor, 0u));
   __syncthreads();
 
-#pragma unroll 1
-  for (int64_t cb = c0; cb < c1; cb += CHUNK) {
-    const int64_t c = cb + (int64_t)VPT * tid;
-    const int nvalid = (int)max((int64_t)0, min((int64_t)VPT, c1 - c));
-    float x[VPT];
-    if (F32)
-      load_logits8_f32<VEC>((const float*)a.logits + r * a.logits_stride, c, nvalid, x);
-    else
-      load_logits8<VEC>((const uint16_t*)a.logits + r * a.logits_stride, c, nvalid, x);
-    const float thr = sm.thr;
-    K key[VPT];
+  K* q = st.queue[warp];
+  WarpTopK<K> w;
+  wtk_init(w, st.lists[warp], kFiniteFloor, lane);
+
+  auto consume = [&](const float (&x)[VPT], int64_t c, int nvalid) {
+    wtk_adopt(w, &st.cut, lane);
+    const float thr = w.thr;
     unsigned m = 0;
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) {
-      key[j] = make_key<K>(x[j], (int)(c + j - c0));
+    for (int j = 0; j < VPT; ++j)
       if (j < nvalid && x[j] >= thr) m |= 1u << j;
+    if (__any_sync(kFull, m)) {
+      K key[VPT];
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) {
+        const int local = (int)(c + j - c0);
+        if (F32)
+          key[j] = (K)(((uint64_t)enc32(x[j]) << 32) | (uint64_t)(0xffffffffu - (uint32_t)local));
+        else
+          key[j] = (K)((enc16(f2bf(x[j])) << 16) | (uint32_t)(0xffff - local));
+      }
+      wtk_push(w, q, key, m, lane);
     }
-    cand_push<K>(sm.buf, &sm.cnt, key, m, lane);
-    __syncthreads();
-    const bool full = sm.cnt > CAP - CHUNK;
-    __syncthreads();
-    if (full) cand_compact<K>(sm.buf, &sm.cnt, &sm.thr, sm.top, &sm.tcnt, sm.hist, sm.bcast);
+    if (w.qn >= kMaxK) {
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane), st.v16, warp, lane);
+      if (t > w.thr) wtk_raise(w, &st.cut, t, 0u, lane);
+    }
+  };
+
+  const int ngroups = (int)((c1 - c0 + GROUP - 1) / GROUP);
+  auto gcol = [&](int g) { return c0 + (int64_t)g * GROUP + (int64_t)VPT * lane; };
+  auto gvalid = [&](int g) { return (int)max((int64_t)0, min((int64_t)VPT, c1 - gcol(g))); };
+  auto prefetch_group = [&](int g) {
+    if (!VEC || lane != 0 || g >= ngroups) return;
+    const int64_t cc = c0 + (int64_t)g * GROUP;
+    if (cc + GROUP <= c1) prefetch_l2(xrow + cc * EB, GROUP * EB);
+  };
+  for (int k = 1; k <= PF_GROUPS; ++k) prefetch_group(warp + k * NW);
+
+  float xa[VPT], xb[VPT];
+  if (warp < ngroups) load_vals8<F32, VEC>(xrow, gcol(warp), gvalid(warp), xa);
+  for (int g = warp; g < ngroups; g += NW) {
+    const bool more = g + NW < ngroups;
+    if (more) load_vals8<F32, VEC>(xrow, gcol(g + NW), gvalid(g + NW), xb);
+    prefetch_group(g + (PF_GROUPS + 1) * NW);
+    consume(xa, gcol(g), gvalid(g));
+    if (more) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j) xa[j] = xb[j];
+    }
   }
   pdl_trigger();
 
-  uint64_t* lists = cand + (uint64_t)r * splits * kMaxK;
-  split_finish<K>(sm.buf, &sm.cnt, &sm.thr, sm.top, &sm.tcnt, sm.hist, sm.bcast, c0,
-                  lists + (int64_t)split * kMaxK);
-  if (!arrive_last(tickets + r, splits, &sm.flag)) return;
-  if (warp != 0) return;
+  if (w.qn) wtk_absorb(w, q, lane);
+  K fin[4];
+  block_fold(st.lists, warp, lane, fin);
+  if (warp == 0) {
+    const K last = __shfl_sync(kFull, fin[3], 31);
+    if (lane == 0) st.flag = last != 0;
+  }
+  __syncthreads();
+  if (!st.flag) {
+    // fewer than 128 finite values in this split: redo it keeping -inf
+    if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
+    __syncthreads();
+    wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
+    for (int gg = warp; gg < ngroups; gg += NW) {
+      float x[VPT];
+      load_vals8<F32, VEC>(xrow, gcol(gg), gvalid(gg), x);
+      consume(x, gcol(gg), gvalid(gg));
+    }
+    if (w.qn) wtk_absorb(w, q, lane);
+    block_fold(st.lists, warp, lane, fin);
+  }
+  uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
+  if (warp == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) stcg64(lists + (int64_t)split * kMaxK + 4 * lane + j, to_global<K>(fin[j], c0));
+    __threadfence();
+  }
+  if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
 
   uint64_t k[4];
-  warp_fold_lists(lists, splits, lane, k);
+  block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
+  if (warp != 0) return;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int i = 4 * lane + j;
     if (i >= a.k) continue;
     const uint32_t e = (uint32_t)(k[j] >> 32);
-    const int64_t col = (int64_t)(0xffffffffu - (uint32_t)k[j]);
+    const int64_t col = key_column(k[j]);
     const int64_t o = r * a.k + i;
-    const float val = F32 ? dec32(e) : bf2f(dec16(e));
+    const float val = F32 ? dec32(e) : bf2f((uint16_t)dec16(e));
     if (a.values_dtype == SONIC_DTYPE_F32)
       ((float*)a.values)[o] = val;
     else
@@ -735,43 +1455,53 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
 }
 
 // ---------------------------------------------------------------------------------------
-// fused multistep: prologue over all gamma+1 rows of a request (aux rows read once),
-// merge per row, softmax of the masked candidates, chain verification
+// fused multistep: prologue over all gamma+1 rows of a request (count and bias rows read
+// once per request), merge per row, softmax of the masked candidates, chain verification
 // (ops/prologue.py:272 + ops/multistep.py:76 + ops/verify.py:244)
 // ---------------------------------------------------------------------------------------
-
-constexpr int MS_MAX_STEPS = SONIC_MAX_LOOKAHEAD + 1;
-constexpr int MS_GROUP = 8;  // logits rows loaded together per chunk
 
 struct MsSmem {
   int hist[256];
   int bcast[4];
   int cnt[MS_MAX_STEPS];
   float thr[MS_MAX_STEPS];
+  uint32_t vmin2[MS_MAX_STEPS];
+  int warp_over[2][NT / 32];
   int tcnt;
   int flag;
+  int err;
   int32_t drafted[MS_MAX_STEPS];
   unsigned long long best[MS_MAX_STEPS];
   uint32_t top[kMaxK];
+  uint64_t bars[STAGES];
   // after the streaming phase (last CTA only):
   float prob[MS_MAX_STEPS][kMaxK];
   int32_t cand[MS_MAX_STEPS][kMaxK];
   int64_t gsel[MS_MAX_STEPS];
 };
 
-static int ms_cap(int steps) { return steps <= 8 ? 3072 : 2176; }
+__host__ __device__ constexpr size_t ms_state_bytes() { return (sizeof(MsSmem) + 127) / 128 * 128; }
 
-static size_t ms_smem_bytes(int steps) {
-  return sizeof(MsSmem) + (size_t)steps * ms_cap(steps) * sizeof(uint32_t);
+// stage layout of one 1024-column multistep chunk: aux, then per-row logits + grammar bits
+constexpr int MS_D = 0;
+constexpr int MS_C = MS_D + CH_MS * 4;
+constexpr int MS_B = MS_C + CH_MS * 4;
+constexpr int MS_X = MS_B + CH_MS * 2;
+constexpr int MS_STEP = CH_MS * 2 + 128;
+
+__host__ __device__ inline size_t ms_stage_bytes(int steps) { return (size_t)MS_X + (size_t)steps * MS_STEP; }
+
+static size_t ms_smem_bytes(int steps, int mode) {
+  size_t s = ms_state_bytes() + (size_t)steps * CAP_MS * sizeof(uint32_t);
+  if (mode == kTma) s += STAGES * ms_stage_bytes(steps);
+  return s;
 }
 
-template <bool VEC>
-__global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs a, int splits, int cols,
-                                                       int log2bn, int cap, uint64_t* cand,
-                                                       uint32_t* tickets) {
-  extern __shared__ __align__(16) unsigned char smem_raw[];
+template <int MODE>
+__global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs a, int splits, int cols, int log2bn,
+                                                       Workspace ws) {
+  extern __shared__ __align__(128) unsigned char smem_raw[];
   MsSmem& sm = *reinterpret_cast<MsSmem*>(smem_raw);
-  uint32_t* bufs = reinterpret_cast<uint32_t*>(smem_raw + sizeof(MsSmem));
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
   const int64_t b = blockIdx.y;
@@ -798,106 +1528,331 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
     return;
   }
   const uint32_t ind = P.indicators[slot];
-  const Needs nd = row_needs(P, ind);
-  const RowParams rp = load_row_params(P, slot, ind);
+  const RowConsts rc = row_consts(P, slot, ind);
   const bool greedy = (ind & 0x40) != 0;
+  uint32_t* bufs = reinterpret_cast<uint32_t*>(smem_raw + ms_state_bytes());
+  unsigned char* stages = reinterpret_cast<unsigned char*>(bufs + (size_t)(G + 1) * CAP_MS);
+  const size_t stage_bytes = ms_stage_bytes(G + 1);
   if (tid < T) {
     sm.drafted[tid] = a.drafted_tokens[margin + tid];
     sm.cnt[tid] = 0;
-    sm.thr[tid] = __int_as_float(0xff800000);
+    sm.thr[tid] = kFiniteFloor;
+    sm.vmin2[tid] = rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u;
     sm.best[tid] = 0ull;
+  }
+  if (tid == 0) {
+    sm.err = 0;
+    if (MODE == kTma) {
+      for (int s = 0; s < STAGES; ++s) mbar_init(&sm.bars[s], 1);
+      mbar_fence_init();
+    }
   }
   __syncthreads();
 
-#pragma unroll 1
-  for (int64_t cb = c0; cb < c1; cb += CHUNK) {
-    const int64_t c = cb + (int64_t)VPT * tid;
-    const int nvalid = (int)max((int64_t)0, min((int64_t)VPT, c1 - c));
-    Cols8 cc;
+  const int64_t shard = a.shard_offset;
+  const int64_t grow0 = slot * (G + 1);
+  uint32_t compacted = 0;  // bit s: row s had its first compaction (uniform across threads)
+  int parity = 0;
+
+  // process VPT_MS columns [c, c + VPT_MS) of every row of the request; returns the rows
+  // whose buffer count passed its compaction limit (this thread's view)
+  auto consume_rows = [&](int64_t c, int nvalid, const int32_t (&d)[VPT_MS], const int32_t (&cx)[VPT_MS],
+                          const uint32_t (&bb)[VPT_MS / 2], auto&& get_x, auto&& get_g) -> int {
+    int over = 0;
+    for (int s = 0; s < T; ++s) {
+      uint32_t xw[VPT_MS / 2];
+      get_x(s, xw);
+      const uint32_t g = rc.nd.g ? get_g(s) : 0xffu;
+      if (rc.nd.proc || rc.nd.temp) {
 #pragma unroll
-    for (int j = 0; j < VPT; ++j) cc.col[j] = c + j + a.shard_offset;
-    Aux8 ax;
-    if (nd.proc) load_aux8<VEC>(P, nd, slot, cc, nvalid, ax);
-#pragma unroll 1
-    for (int s0 = 0; s0 < T; s0 += MS_GROUP) {
-      // issue the logits loads of up to MS_GROUP rows before touching any of them
-      float xs[MS_GROUP][VPT];
-#pragma unroll
-      for (int g = 0; g < MS_GROUP; ++g)
-        if (s0 + g < T)
-          load_logits8<VEC>((const uint16_t*)a.logits + (margin + s0 + g) * a.logits_stride, c, nvalid, xs[g]);
-#pragma unroll
-      for (int g = 0; g < MS_GROUP; ++g) {
-        const int s = s0 + g;
-        if (s >= T) break;
-        float (&x)[VPT] = xs[g];
-        if (nd.proc || nd.temp) {
-          const uint32_t gb = nd.g ? load_gbits8<VEC>(P, slot * (G + 1) + s, cc, nvalid) : 0xffu;
-#pragma unroll
-          for (int j = 0; j < VPT; ++j) {
-            int32_t dec = nd.proc ? ax.dec[j] : 0;
-            if (nd.dec)
-              for (int q = 0; q < s; ++q) dec += (sm.drafted[q] == cc.col[j]);
-            x[j] = apply_processors(x[j], ind, nd, (gb >> j) & 1u, dec, nd.proc ? ax.ctx[j] : 0,
-                                    nd.proc ? ax.bias[j] : 0.0f, rp);
-          }
-        }
-        if (greedy) {
-          uint64_t best = 0;
-#pragma unroll
-          for (int j = 0; j < VPT; ++j)
-            if (j < nvalid) best = umax(best, greedy_key(x[j], c + j, log2bn));
-          best = warp_max_u64(best);
-          if (lane == 0 && best) atomicMax(&sm.best[s], (unsigned long long)best);
-        } else {
-          const float thr = sm.thr[s];
-          uint32_t key[VPT];
-          unsigned m = 0;
-#pragma unroll
-          for (int j = 0; j < VPT; ++j) {
-            key[j] = make_key<uint32_t>(x[j], (int)(c + j - c0));
-            if (j < nvalid && x[j] >= thr) m |= 1u << j;
-          }
-          cand_push<uint32_t>(bufs + (int64_t)s * cap, &sm.cnt[s], key, m, lane);
+        for (int p = 0; p < VPT_MS / 2; ++p) {
+          int32_t d0 = d[2 * p], d1 = d[2 * p + 1];
+          if (rc.nd.dec)
+            for (int q = 0; q < s; ++q) {
+              d0 += (sm.drafted[q] == c + 2 * p + shard);
+              d1 += (sm.drafted[q] == c + 2 * p + 1 + shard);
+            }
+          xw[p] = process_pair(xw[p], (g >> (2 * p)) & 3u, d0, d1, cx[2 * p], cx[2 * p + 1], bb[p], rc);
         }
       }
+      if (greedy) {
+        uint64_t best = 0;
+#pragma unroll
+        for (int j = 0; j < VPT_MS; ++j)
+          if (j < nvalid) best = umax(best, greedy_key_bits(half_of(xw, j), c + j, log2bn));
+        best = warp_max_u64(best);
+        if (lane == 0 && best) atomicMax(&sm.best[s], (unsigned long long)best);
+      } else {
+        const float thr = sm.thr[s];
+        uint32_t key[VPT];
+        unsigned m = 0;
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          key[j] = 0;
+          if (j < VPT_MS) {
+            const uint32_t h = half_of(xw, j);
+            key[j] = (enc16(h) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
+            if (j < nvalid && bf2f((uint16_t)h) >= thr) m |= 1u << j;
+          }
+        }
+        const int end = cand_push<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], key, m, lane);
+        const int lim = ((compacted >> s) & 1u) ? CAP_MS - CH_MS : kMaxK;
+        if (end > lim) over |= 1 << s;
+      }
     }
-    if (!greedy) {
+    return over;
+  };
+
+  // block-wide OR of the per-thread masks; one barrier (double-buffered warp slots)
+  auto block_or = [&](int over) -> int {
+    const int v = (int)__reduce_or_sync(kFull, (unsigned)over);
+    if (lane == 0) sm.warp_over[parity][warp] = v;
+    __syncthreads();
+    int res = 0;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) res |= sm.warp_over[parity][w];
+    parity ^= 1;
+    return res;
+  };
+
+  auto compact_rows = [&](int full) {
+    for (int s = 0; s < T; ++s)
+      if ((full >> s) & 1) {
+        cand_compact<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt, sm.hist,
+                               sm.bcast);
+        if (tid == 0 && rc.fast) sm.vmin2[s] = vmin_pair(sm.thr[s], rc);
+      }
+    compacted |= (uint32_t)full;
+    if (rc.fast) __syncthreads();
+  };
+
+  // fast path (see vmin_pair): one thread's 4 columns of every row straight from the stage
+  auto fast_rows = [&](unsigned char* sp, int64_t c) -> int {
+    const int32_t* sd = reinterpret_cast<const int32_t*>(sp + MS_D) + VPT_MS * tid;
+    const int32_t* sc = reinterpret_cast<const int32_t*>(sp + MS_C) + VPT_MS * tid;
+    uint32_t base_need = 0;
+    if (rc.nd.dec) {
+      const uint4 d4 = *reinterpret_cast<const uint4*>(sd);
+      uint32_t nz[VPT_MS] = {d4.x, d4.y, d4.z, d4.w};
+      if (rc.nd.ctx) {
+        const uint4 c4 = *reinterpret_cast<const uint4*>(sc);
+        nz[0] |= c4.x; nz[1] |= c4.y; nz[2] |= c4.z; nz[3] |= c4.w;
+      }
+#pragma unroll
+      for (int j = 0; j < VPT_MS; ++j) base_need |= (uint32_t)(nz[j] != 0u) << j;
+    }
+    uint2 bq = make_uint2(0u, 0u);
+    if (rc.nd.bias) bq = *reinterpret_cast<const uint2*>(sp + MS_B + 8 * tid);
+    int over = 0;
+    for (int s = 0; s < T; ++s) {
+      unsigned char* row = sp + MS_X + s * MS_STEP;
+      uint32_t* sx = reinterpret_cast<uint32_t*>(row) + 2 * tid;
+      if (rc.nd.dec) {
+        uint32_t need = base_need;
+        for (int q = 0; q < s; ++q) {
+          const int64_t dl = (int64_t)sm.drafted[q] - (c + shard);
+          if (dl >= 0 && dl < VPT_MS) need |= 1u << dl;
+        }
+        while (need) {
+          const int j = __ffs(need) - 1;
+          need &= need - 1;
+          int32_t dj = sd[j];
+          for (int q = 0; q < s; ++q) dj += (sm.drafted[q] == c + j + shard);
+          uint16_t* xp = reinterpret_cast<uint16_t*>(sx) + j;
+          *xp = (uint16_t)repetition_one(*xp, dj, rc.nd.ctx ? sc[j] : 0, rc);
+        }
+      }
+      const uint2 xq = *reinterpret_cast<const uint2*>(sx);
+      uint32_t x[2] = {xq.x, xq.y};
+      if (rc.nd.bias) {
+        x[0] = bf2_add(x[0], bq.x);
+        x[1] = bf2_add(x[1], bq.y);
+      }
+      uint32_t m = ge_mask4(x, sm.vmin2[s]);
+      if (rc.nd.g) m &= (uint32_t)(row[CH_MS * 2 + (tid >> 1)] >> (4 * (tid & 1)));
+      int end = 0;
+      if (m) {
+        *reinterpret_cast<uint2*>(sx) = make_uint2(x[0], x[1]);
+        while (m) {
+          const int j = __ffs(m) - 1;
+          m &= m - 1;
+          const float fv = final_value(bf2f(reinterpret_cast<const uint16_t*>(sx)[j]), rc);
+          if (fv == fv && fabsf(fv) <= 3.3895313892515355e+38f) {
+            const uint32_t key = (enc16(f2bf(fv)) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
+            const int pos = atomicAdd(&sm.cnt[s], 1);
+            if (pos < CAP_MS) bufs[(size_t)s * CAP_MS + pos] = key;
+            end = pos + 1;
+          }
+        }
+      }
+      const int lim = ((compacted >> s) & 1u) ? CAP_MS - CH_MS : kMaxK;
+      if (end > lim) over |= 1 << s;
+    }
+    return over;
+  };
+
+  auto direct_chunk = [&](int64_t cb) -> int {
+    constexpr int DM = (MODE == kTma) ? kVec : MODE;
+    const int64_t c = cb + (int64_t)VPT_MS * tid;
+    const int nvalid = (int)max((int64_t)0, min((int64_t)VPT_MS, c1 - c));
+    int32_t d[VPT_MS] = {0, 0, 0, 0}, cx[VPT_MS] = {0, 0, 0, 0};
+    uint32_t bb[VPT_MS / 2] = {0, 0};
+    if (rc.nd.proc) {
+#pragma unroll
+      for (int j = 0; j < VPT_MS; ++j) {
+        const bool ok = j < nvalid;
+        const int64_t col = c + j + shard;
+        if (rc.nd.dec && ok) d[j] = __ldcs(P.decode_counts + slot * P.counts_stride + col);
+        if (rc.nd.ctx && ok) cx[j] = __ldcs(P.context_counts + slot * P.counts_stride + col);
+        if (rc.nd.bias && ok) bb[j >> 1] |= (uint32_t)__ldcs(P.bias + slot * P.bias_stride + col) << (16 * (j & 1));
+      }
+    }
+    auto get_x = [&](int s, uint32_t (&xw)[VPT_MS / 2]) {
+      const uint16_t* xr = (const uint16_t*)a.logits + (margin + s) * a.logits_stride;
+      if (DM == kVec && nvalid == VPT_MS) {
+        const uint2 q = __ldcs(reinterpret_cast<const uint2*>(xr + c));
+        xw[0] = q.x;
+        xw[1] = q.y;
+      } else {
+#pragma unroll
+        for (int p = 0; p < VPT_MS / 2; ++p) {
+          const uint32_t lo = (2 * p < nvalid) ? (uint32_t)__ldcs(xr + c + 2 * p) : 0xff80u;
+          const uint32_t hi = (2 * p + 1 < nvalid) ? (uint32_t)__ldcs(xr + c + 2 * p + 1) : 0xff80u;
+          xw[p] = lo | (hi << 16);
+        }
+      }
+    };
+    auto get_g = [&](int s) -> uint32_t {
+      const uint32_t* g = P.grammar + (grow0 + s) * P.grammar_stride;
+      uint32_t bits = 0;
+#pragma unroll
+      for (int j = 0; j < VPT_MS; ++j)
+        if (j < nvalid) bits |= ((__ldg(g + ((c + j + shard) >> 5)) >> ((c + j + shard) & 31)) & 1u) << j;
+      return bits;
+    };
+    return consume_rows(c, nvalid, d, cx, bb, get_x, get_g);
+  };
+
+  int64_t cb = c0;
+  if (MODE == kTma) {
+    const int nfull = (int)((c1 - c0) / CH_MS);
+    const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
+    const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
+    const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
+    const uint32_t tx = (drow ? CH_MS * 4 : 0) + (crow ? CH_MS * 4 : 0) + (brow ? CH_MS * 2 : 0) +
+                        (uint32_t)T * (CH_MS * 2 + (rc.nd.g ? CH_MS / 8 : 0));
+    auto issue = [&](int i) {
+      unsigned char* sp = stages + (size_t)(i % STAGES) * stage_bytes;
+      uint64_t* bar = &sm.bars[i % STAGES];
+      const int64_t cc = c0 + (int64_t)i * CH_MS;
+      mbar_expect_tx(bar, tx);
+      if (drow) bulk_load(sp + MS_D, drow + cc + shard, CH_MS * 4, bar);
+      if (crow) bulk_load(sp + MS_C, crow + cc + shard, CH_MS * 4, bar);
+      if (brow) bulk_load(sp + MS_B, brow + cc + shard, CH_MS * 2, bar);
+      for (int s = 0; s < T; ++s) {
+        const uint16_t* xr = (const uint16_t*)a.logits + (margin + s) * a.logits_stride;
+        bulk_load(sp + MS_X + s * MS_STEP, xr + cc, CH_MS * 2, bar);
+        if (rc.nd.g)
+          bulk_load(sp + MS_X + s * MS_STEP + CH_MS * 2,
+                    P.grammar + (grow0 + s) * P.grammar_stride + (cc + shard) / 32, CH_MS / 8, bar);
+      }
+    };
+    if (tid == 0)
+      for (int i = 0; i < min(nfull, STAGES); ++i) issue(i);
+    for (int i = 0; i < nfull; ++i) {
+      const unsigned char* sp = stages + (size_t)(i % STAGES) * stage_bytes;
+      if (!sm.err && !mbar_wait_bounded(&sm.bars[i % STAGES], (uint32_t)(i / STAGES) & 1u, WAIT_LIMIT)) sm.err = 1;
+      const int64_t c = cb + (int64_t)VPT_MS * tid;
+      if (rc.fast) {
+        const int full = block_or(fast_rows(const_cast<unsigned char*>(sp), c));
+        if (tid == 0 && i + STAGES < nfull) {
+          fence_proxy_async();
+          issue(i + STAGES);
+        }
+        if (full) compact_rows(full);
+        cb += CH_MS;
+        continue;
+      }
+      int32_t d[VPT_MS] = {0, 0, 0, 0}, cx[VPT_MS] = {0, 0, 0, 0};
+      uint32_t bb[VPT_MS / 2] = {0, 0};
+      if (rc.nd.dec) {
+        const uint4 q = *reinterpret_cast<const uint4*>(sp + MS_D + tid * 16);
+        d[0] = q.x; d[1] = q.y; d[2] = q.z; d[3] = q.w;
+      }
+      if (rc.nd.ctx) {
+        const uint4 q = *reinterpret_cast<const uint4*>(sp + MS_C + tid * 16);
+        cx[0] = q.x; cx[1] = q.y; cx[2] = q.z; cx[3] = q.w;
+      }
+      if (rc.nd.bias) {
+        const uint2 q = *reinterpret_cast<const uint2*>(sp + MS_B + tid * 8);
+        bb[0] = q.x;
+        bb[1] = q.y;
+      }
+      auto get_x = [&](int s, uint32_t (&xw)[VPT_MS / 2]) {
+        const uint2 q = *reinterpret_cast<const uint2*>(sp + MS_X + s * MS_STEP + tid * 8);
+        xw[0] = q.x;
+        xw[1] = q.y;
+      };
+      auto get_g = [&](int s) -> uint32_t {
+        // thread t's 4 columns are bits 4(t & 1) .. 4(t & 1) + 3 of grammar byte t / 2
+        const uint32_t byte = sp[MS_X + s * MS_STEP + CH_MS * 2 + (tid >> 1)];
+        return (byte >> (4 * (tid & 1))) & 0xfu;
+      };
+      const int full = block_or(consume_rows(c, VPT_MS, d, cx, bb, get_x, get_g));
+      if (tid == 0 && i + STAGES < nfull) {
+        fence_proxy_async();
+        issue(i + STAGES);
+      }
+      if (!greedy && full) compact_rows(full);
+      cb += CH_MS;
+    }
+  }
+  for (; cb < c1; cb += CH_MS) {
+    const int full = block_or(direct_chunk(cb));
+    if (!greedy && full) compact_rows(full);
+  }
+  // rows with fewer than 128 finite candidates in this split: redo them keeping -inf
+  if (!greedy) {
+    __syncthreads();
+    int redo = 0;
+    for (int s = 0; s < T; ++s)
+      if (sm.cnt[s] < kMaxK) redo |= 1 << s;
+    __syncthreads();
+    if (redo) {
+      if (tid < T) {
+        sm.cnt[tid] = 0;
+        sm.thr[tid] = __int_as_float(0xff800000);
+      }
+      compacted = 0xffffffffu;
       __syncthreads();
-      unsigned full = 0;
-      for (int s = 0; s < T; ++s)
-        if (sm.cnt[s] > cap - CHUNK) full |= 1u << s;
-      __syncthreads();
-#pragma unroll 1
-      for (int s = 0; s < T; ++s)
-        if ((full >> s) & 1u)
-          cand_compact<uint32_t>(bufs + (int64_t)s * cap, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt,
-                                 sm.hist, sm.bcast);
+      for (int64_t cc = c0; cc < c1; cc += CH_MS) {
+        const int full = block_or(direct_chunk(cc));
+        if (full) compact_rows(full);
+      }
     }
   }
   pdl_trigger();
+  __syncthreads();
+  if (sm.err) {
+    if (tid == 0) atomicOr(ws.error, 1u);
+    return;
+  }
 
-  // per-row candidate lists: row (margin + s), split
-  const int64_t L = a.total_rows;
-  (void)L;
   if (greedy) {
-    __syncthreads();
     if (tid < T) {
-      __stcg(reinterpret_cast<unsigned long long*>(cand + ((margin + tid) * splits + split) * kMaxK), sm.best[tid]);
+      stcg64(ws.cand + ((margin + tid) * splits + split) * kMaxK, sm.best[tid]);
       __threadfence();
     }
   } else {
-#pragma unroll 1
     for (int s = 0; s < T; ++s)
-      split_finish<uint32_t>(bufs + (int64_t)s * cap, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt, sm.hist,
-                             sm.bcast, c0, cand + ((margin + s) * splits + split) * kMaxK);
+      split_finish<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt, sm.hist, sm.bcast,
+                             c0, ws.cand + ((margin + s) * splits + split) * kMaxK);
   }
-  if (!arrive_last(tickets + b, splits, &sm.flag)) return;
+  if (!arrive_last(ws.tickets + b, splits, &sm.flag)) return;
 
   // ---- per-row merge (warp w handles rows w, w+8, ...) ----
-  const float ninf = __int_as_float(0xff800000);
   for (int s = warp; s < T; s += NT / 32) {
-    const uint64_t* lists = cand + (margin + s) * splits * kMaxK;
+    const uint64_t* lists = ws.cand + (margin + s) * splits * kMaxK;
     if (greedy) {
       uint64_t bk = 0;
       for (int q = lane; q < splits; q += 32) bk = umax(bk, ldcg64(lists + (int64_t)q * kMaxK));
@@ -914,7 +1869,7 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
       int64_t idx[4];
       decode_keys(k, v, idx);
       const float vmax = __shfl_sync(kFull, v[0], 0);
-      if (ind & 0x380) warp_masking(P, slot, ind, v, vmax, lane);
+      if (ind & 0x380) warp_masking(load_mask_params(P, slot), ind, v, vmax, lane);
       float ls[4];
       warp_log_softmax(v, vmax, ls);
 #pragma unroll
@@ -930,7 +1885,6 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
   }
   __syncthreads();
   if (warp != 0) return;
-  (void)ninf;
 
   // ---- chain verification (verify.py:244-434), one warp ----
   const uint32_t flags = a.flags;
@@ -1016,7 +1970,8 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
           for (int j = 0; j < 4; ++j) {
             const int i = 4 * lane + j;
             if (i < z) {
-              store_float(a.top_logprob_values, a.logprobs_dtype, (margin + s) * a.top_stride + i, dlog(sm.prob[s][i]));
+              store_float(a.top_logprob_values, a.logprobs_dtype, (margin + s) * a.top_stride + i,
+                          dlog(sm.prob[s][i]));
               a.top_logprob_tokens[(margin + s) * a.top_stride + i] = sm.cand[s][i];
             }
           }
@@ -1056,6 +2011,8 @@ static int ilog2(int v) {
 
 template <typename Kern, typename... Args>
 static cudaError_t launch(Kern kern, dim3 grid, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(NT);
@@ -1082,7 +2039,7 @@ static sonic_status check_block_n(int32_t block_n) {
   return SONIC_OK;
 }
 
-// Vector (16-byte) aux loads need every row start and column offset 32-byte aligned.
+// 16-byte vector loads of aux rows: every row start and column offset 32-byte aligned
 static bool params_vec_ok(const SonicSamplingParams& P, int64_t shard_offset) {
   bool ok = (shard_offset % 32) == 0;
   if (P.decode_counts) ok = ok && aligned(P.decode_counts, 16) && (P.counts_stride % 4) == 0;
@@ -1091,11 +2048,25 @@ static bool params_vec_ok(const SonicSamplingParams& P, int64_t shard_offset) {
   return ok;
 }
 
+// bulk copies additionally read grammar words in 16-byte groups
+static bool params_tma_ok(const SonicSamplingParams& P, int64_t shard_offset) {
+  bool ok = params_vec_ok(P, shard_offset) && (shard_offset % 128) == 0;
+  if (P.grammar) ok = ok && aligned(P.grammar, 16) && (P.grammar_stride % 4) == 0;
+  return ok;
+}
+
 static sonic_status check_params(const SonicSamplingParams& P) {
   if (!P.indicators) return fail(SONIC_ERR_INVALID_ARGUMENT, "indicators must not be NULL");
   if (P.slot_mapping && P.slot_dtype != SONIC_DTYPE_I32 && P.slot_dtype != SONIC_DTYPE_I64)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "slot_mapping dtype must be i32 or i64");
   return SONIC_OK;
+}
+
+static Plan singular_plan(int64_t rows, int64_t V) { return split_plan(rows, V, CH); }
+static Plan multistep_plan(int64_t batch, int64_t V) { return split_plan(batch, V, CH_MS); }
+
+static int64_t multistep_rows(const SonicMultistepArgs* a) {
+  return a->total_rows > 0 ? a->total_rows : (int64_t)a->batch_size * (a->lookahead + 1);
 }
 
 }  // namespace sonic
@@ -1109,22 +2080,18 @@ int32_t sonic_abi_version(void) { return SONIC_B200_ABI_VERSION; }
 const char* sonic_last_error(void) { return g_last_error.c_str(); }
 
 size_t sonic_fused_singular_workspace_size(const SonicSingularArgs* a) {
-  return a ? workspace_bytes(a->rows, a->vocab_size) : 0;
+  if (!a || a->rows <= 0) return 0;
+  return workspace_bytes(a->rows, a->rows, singular_plan(a->rows, a->vocab_size).splits);
 }
 
 size_t sonic_fused_multistep_workspace_size(const SonicMultistepArgs* a) {
-  if (!a) return 0;
-  // candidate lists per row, tickets per request
-  if (a->batch_size <= 0) return 0;
-  Plan p = split_plan(a->batch_size, a->vocab_size);
-  int64_t rows = a->total_rows > 0 ? a->total_rows : (int64_t)a->batch_size * (a->lookahead + 1);
-  size_t cand = (size_t)rows * p.splits * kMaxK * sizeof(uint64_t);
-  size_t tick = (size_t)a->batch_size * sizeof(uint32_t);
-  return cand + ((tick + 255) / 256) * 256;
+  if (!a || a->batch_size <= 0) return 0;
+  return workspace_bytes(multistep_rows(a), a->batch_size, multistep_plan(a->batch_size, a->vocab_size).splits);
 }
 
 size_t sonic_bounded_topk_workspace_size(const SonicTopKArgs* a) {
-  return a ? workspace_bytes(a->rows, a->vocab_size) : 0;
+  if (!a || a->rows <= 0) return 0;
+  return workspace_bytes(a->rows, a->rows, singular_plan(a->rows, a->vocab_size).splits);
 }
 
 sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
@@ -1145,32 +2112,36 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel noise must not be NULL without SONIC_FLAG_PHILOX");
   if ((a->flags & SONIC_FLAG_UPDATE_COUNTS) && !a->params.decode_counts)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "`update_counts` is True but `decode_counts` is None");
-  if ((a->flags & SONIC_FLAG_PROBABILITIES) && a->probabilities &&
-      a->probabilities_dtype != SONIC_DTYPE_BF16 && a->probabilities_dtype != SONIC_DTYPE_F32)
+  if ((a->flags & SONIC_FLAG_PROBABILITIES) && a->probabilities && a->probabilities_dtype != SONIC_DTYPE_BF16 &&
+      a->probabilities_dtype != SONIC_DTYPE_F32)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "probabilities dtype must be bf16 or f32");
   if (a->max_top_logprobs < 0 || a->max_top_logprobs > kMaxK)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "max_top_logprobs must be in [0, 128]");
   if (a->logprobs_dtype != SONIC_DTYPE_BF16 && a->logprobs_dtype != SONIC_DTYPE_F32)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logprobs dtype must be bf16 or f32");
-  const size_t need = workspace_bytes(a->rows, a->vocab_size);
+  const Plan p = singular_plan(a->rows, a->vocab_size);
+  const size_t need = workspace_bytes(a->rows, a->rows, p.splits);
   if (!a->workspace || a->workspace_bytes < need)
     return fail(SONIC_ERR_WORKSPACE, "workspace smaller than sonic_fused_singular_workspace_size()");
-  Plan p = split_plan(a->rows, a->vocab_size);
-  uint64_t* cand = (uint64_t*)a->workspace;
-  uint32_t* tick = (uint32_t*)((char*)a->workspace + (size_t)a->rows * p.splits * kMaxK * sizeof(uint64_t));
-  const bool vec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0 && params_vec_ok(a->params, a->shard_offset);
+  const Workspace ws = carve(a->workspace, a->rows, a->rows, p.splits);
+  const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
   const bool ind = a->d2t != nullptr;
+  int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
+  if (mode == kVec && !ind && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
   dim3 grid(p.splits, a->rows);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
+  const size_t ring = mode == kTma ? (size_t)NW * WST * WS_BYTES : 0;
   cudaError_t e;
   if (ind)
-    e = vec ? launch(singular_kernel<true, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, cand, tick)
-            : launch(singular_kernel<false, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, cand, tick);
+    e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws)
+                     : launch(singular_kernel<kScalar, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws);
+  else if (mode == kTma)
+    e = launch(singular_kernel<kTma, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws);
   else
-    e = vec ? launch(singular_kernel<true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, cand, tick)
-            : launch(singular_kernel<false, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, cand, tick);
+    e = mode == kVec ? launch(singular_kernel<kVec, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws)
+                     : launch(singular_kernel<kScalar, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws);
   return check_launch(e, "sonic_fused_singular");
 }
 
@@ -1187,29 +2158,23 @@ sonic_status sonic_bounded_topk(const SonicTopKArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "values must be a non-NULL bf16 or f32 tensor");
   if (!a->indices || (a->indices_dtype != SONIC_DTYPE_I32 && a->indices_dtype != SONIC_DTYPE_I64))
     return fail(SONIC_ERR_INVALID_ARGUMENT, "indices must be a non-NULL i32 or i64 tensor");
-  const size_t need = workspace_bytes(a->rows, a->vocab_size);
+  const Plan p = singular_plan(a->rows, a->vocab_size);
+  const size_t need = workspace_bytes(a->rows, a->rows, p.splits);
   if (!a->workspace || a->workspace_bytes < need)
     return fail(SONIC_ERR_WORKSPACE, "workspace smaller than sonic_bounded_topk_workspace_size()");
-  Plan p = split_plan(a->rows, a->vocab_size);
-  uint64_t* cand = (uint64_t*)a->workspace;
-  uint32_t* tick = (uint32_t*)((char*)a->workspace + (size_t)a->rows * p.splits * kMaxK * sizeof(uint64_t));
+  const Workspace ws = carve(a->workspace, a->rows, a->rows, p.splits);
   const bool f32 = a->logits_dtype == SONIC_DTYPE_F32;
   const bool vec = aligned(a->logits, 16) && (a->logits_stride % (f32 ? 4 : 8)) == 0;
   dim3 grid(p.splits, a->rows);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   cudaError_t e;
-  if (f32) {
-    const size_t smem = sizeof(RowSmem<uint64_t>);
-    auto k = vec ? topk_kernel<true, true> : topk_kernel<false, true>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) e = launch(k, grid, smem, st, pdl, *a, p.splits, p.cols, cand, tick);
-  } else {
-    const size_t smem = sizeof(RowSmem<uint32_t>);
-    auto k = vec ? topk_kernel<true, false> : topk_kernel<false, false>;
-    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess) e = launch(k, grid, smem, st, pdl, *a, p.splits, p.cols, cand, tick);
-  }
+  if (f32)
+    e = vec ? launch(topk_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, ws)
+            : launch(topk_kernel<kScalar, true>, grid, 0, st, pdl, *a, p.splits, p.cols, ws);
+  else
+    e = vec ? launch(topk_kernel<kVec, false>, grid, 0, st, pdl, *a, p.splits, p.cols, ws)
+            : launch(topk_kernel<kScalar, false>, grid, 0, st, pdl, *a, p.splits, p.cols, ws);
   return check_launch(e, "sonic_bounded_topk");
 }
 
@@ -1227,8 +2192,7 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logits must be a non-NULL bf16 tensor");
   if (!a->drafted_tokens || !a->tokens || !a->offsets)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "drafted_tokens, tokens and offsets must not be NULL");
-  if (!a->gumbel || !a->uniform)
-    return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel and uniform noise must not be NULL");
+  if (!a->gumbel || !a->uniform) return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel and uniform noise must not be NULL");
   if (a->draft_probs && a->draft_dtype != SONIC_DTYPE_F32 && a->draft_dtype != SONIC_DTYPE_BF16)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "draft probabilities dtype must be f32 or bf16");
   if ((a->flags & SONIC_FLAG_UPDATE_COUNTS) && !a->params.decode_counts)
@@ -1237,23 +2201,30 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "max_top_logprobs must be in [0, 128]");
   if (a->logprobs_dtype != SONIC_DTYPE_BF16 && a->logprobs_dtype != SONIC_DTYPE_F32)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logprobs dtype must be bf16 or f32");
-  const size_t need = sonic_fused_multistep_workspace_size(a);
+  const Plan p = multistep_plan(a->batch_size, a->vocab_size);
+  const int64_t rows = multistep_rows(a);
+  const size_t need = workspace_bytes(rows, a->batch_size, p.splits);
   if (!a->workspace || a->workspace_bytes < need)
     return fail(SONIC_ERR_WORKSPACE, "workspace smaller than sonic_fused_multistep_workspace_size()");
-  Plan p = split_plan(a->batch_size, a->vocab_size);
-  const int64_t rows = a->total_rows > 0 ? a->total_rows : (int64_t)a->batch_size * (a->lookahead + 1);
-  uint64_t* cand = (uint64_t*)a->workspace;
-  uint32_t* tick = (uint32_t*)((char*)a->workspace + (size_t)rows * p.splits * kMaxK * sizeof(uint64_t));
-  const bool vec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0 && params_vec_ok(a->params, a->shard_offset);
+  const Workspace ws = carve(a->workspace, rows, a->batch_size, p.splits);
+  const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
   const int steps = a->lookahead + 1;
-  const int cap = ms_cap(steps);
-  const size_t smem = ms_smem_bytes(steps);
+  int mode = kScalar;
+  if (xvec && params_vec_ok(a->params, a->shard_offset)) mode = kVec;
+  if (mode == kVec && params_tma_ok(a->params, a->shard_offset) && ms_smem_bytes(steps, kTma) <= 200 * 1024)
+    mode = kTma;
+  const size_t smem = ms_smem_bytes(steps, mode);
   dim3 grid(p.splits, a->batch_size);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
-  auto k = vec ? multistep_kernel<true> : multistep_kernel<false>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e == cudaSuccess) e = launch(k, grid, smem, st, pdl, *a, p.splits, p.cols, ilog2(a->block_n), cap, cand, tick);
+  const int l2 = ilog2(a->block_n);
+  cudaError_t e;
+  if (mode == kTma)
+    e = launch(multistep_kernel<kTma>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
+  else if (mode == kVec)
+    e = launch(multistep_kernel<kVec>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
+  else
+    e = launch(multistep_kernel<kScalar>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
   return check_launch(e, "sonic_fused_multistep");
 }
 

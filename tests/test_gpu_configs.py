@@ -1,0 +1,437 @@
+"""CUDA path against the CPU oracle at the benchmark configs' full sizes and on the edge
+cases of the domain. Integer outputs (tokens, offsets, counts, candidate ids) must match
+bit for bit; logprobs and probabilities too, since the kernels and the oracle share one
+fixed fp32 operation order (tests/test_oracle_golden.py pins that oracle to the reference
+within 1e-5)."""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+
+from sonic_sampler_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+BF16, F32, I32 = torch.bfloat16, torch.float32, torch.int32
+
+
+@pytest.fixture(scope="module")
+def dev():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    from sonic_sampler_b200 import _abi
+
+    _abi.load_library()
+    return torch.device("cuda", 0)
+
+
+def bits(t):
+    t = t.detach().cpu()
+    if t.dtype == BF16:
+        return t.view(torch.int16)
+    if t.dtype == F32:
+        return t.view(torch.int32)
+    return t
+
+
+def host(d: dict) -> dict:
+    return {k: (v.detach().cpu().clone() if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
+
+
+def buffer_kwargs(b, timestep: int | None = 0, draft: bool = False) -> dict:
+    """fused_singular / fused_multistep keywords from a SamplingBuffers object (as the
+    modular interface passes them)."""
+    g = b.weights.gumbel.draft if draft else b.weights.gumbel.target
+    kw = dict(
+        indicators=b.flags.draft if draft else b.flags.target,
+        grammar=b.grammar if timestep is None else b.grammar[:, timestep],
+        context_counts=b.repetition.counts.context, decode_counts=b.repetition.counts.decode,
+        repetition_penalties=b.repetition.multiplicative, frequency_penalties=b.repetition.frequency,
+        presence_penalties=b.repetition.presence, logit_bias=b.bias, temperature=b.temperature, top_k=b.top_k,
+        top_p=b.top_p, min_p=b.min_p, top_k_logprobs=b.top_logprobs,
+        gumbel_noise=g if timestep is None else g[:, timestep],
+    )
+    if timestep is None:  # multistep: acceptance uniforms come from the buffers too
+        kw["uniform_noise"] = b.weights.uniform
+    return kw
+
+
+def run_singular(logits, **kw):
+    """(gpu selection, oracle selection, gpu kwargs, host kwargs)."""
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.singular import fused_singular, prepare_singular
+
+    kh = host(kw)
+    sel = fused_singular(logits, **kw)
+    ref, args = prepare_singular(logits.detach().cpu().clone(), **kh)
+    oracle.fused_singular(args)
+    torch.cuda.synchronize()
+    return sel, ref, kw, kh
+
+
+def assert_selection_equal(sel, ref, kw=None, kh=None):
+    assert torch.equal(sel.tokens.cpu(), ref.tokens)
+    if sel.logprobs is not None:
+        stoch = ~(kh["indicators"].to(torch.int32) & 0x40).bool()
+        sm = kh.get("slot_mapping")
+        rows = sel.tokens.size(0)
+        mask = stoch[sm.long()] if sm is not None else stoch[:rows]
+        a, b = sel.logprobs.selected.cpu()[mask], ref.logprobs.selected[mask]
+        nan = torch.isnan(a.float())
+        assert torch.equal(nan, torch.isnan(b.float()))  # fully masked rows: NaN on both sides
+        assert torch.equal(bits(a)[~nan], bits(b)[~nan])
+    if kw is not None and kw.get("decode_counts") is not None:
+        assert torch.equal(kw["decode_counts"].cpu(), kh["decode_counts"])
+    if sel.probabilities is not None:
+        assert torch.equal(bits(sel.probabilities), bits(ref.probabilities))
+
+
+# ----------------------------------------------------------------------------------------
+# config 2: the benchmark workload
+# ----------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("lp_dtype", [BF16, F32])
+def test_config2_full(dev, lp_dtype):
+    w = workloads.config2(dev, seed=5)
+    kw = buffer_kwargs(w["buffers"])
+    sel, ref, kw, kh = run_singular(w["logits"], block_n=4096, update_counts=True, return_logprobs=True,
+                                    max_top_logprobs=5, logprobs_dtype=lp_dtype, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_config2_modular_matches_functional(dev):
+    from sonic_sampler_b200.interface import UnshardedFusedSingular
+
+    w = workloads.config2(dev, seed=6)
+    sampler = UnshardedFusedSingular.initialize(128256, batch_size=64)
+    sel = sampler.autoregressive(w["logits"], w["buffers"], logprobs=True)
+    kw = buffer_kwargs(w["buffers"])
+    _, ref, _, _ = run_singular(w["logits"], block_n=sampler.block_n, return_logprobs=True, max_top_logprobs=5, **kw)
+    assert torch.equal(sel.tokens.cpu(), ref.tokens)
+
+
+def test_config2_repeat_pdl_graph(dev):
+    """Workspace reuse, PDL on/off and CUDA-graph replay all give the same result."""
+    from sonic_sampler_b200.interface import UnshardedFusedSingular
+
+    w = workloads.config2(dev, seed=7)
+    s1 = UnshardedFusedSingular.initialize(128256, batch_size=64, pdl=True)
+    s2 = UnshardedFusedSingular.initialize(128256, batch_size=64, pdl=False)
+    outs = [s1.autoregressive(w["logits"], w["buffers"], logprobs=True) for _ in range(3)]
+    outs.append(s2.autoregressive(w["logits"], w["buffers"], logprobs=True))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        gs = s1.autoregressive(w["logits"], w["buffers"], logprobs=True)
+    g.replay()
+    g.replay()
+    torch.cuda.synchronize()
+    outs.append(gs)
+    for o in outs[1:]:
+        assert torch.equal(o.tokens, outs[0].tokens)
+        assert torch.equal(bits(o.logprobs.selected), bits(outs[0].logprobs.selected))
+
+
+# ----------------------------------------------------------------------------------------
+# config 3: stochastic multistep verification (varlen and fixed)
+# ----------------------------------------------------------------------------------------
+
+
+def run_multistep(logits, tokens, **kw):
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.multistep import fused_multistep, prepare_multistep
+
+    kh = host(kw)
+    ver = fused_multistep(logits, kw["indicators"], tokens, **{k: v for k, v in kw.items() if k != "indicators"})
+    ref, args = prepare_multistep(logits.cpu().clone(), kh["indicators"], tokens.cpu().clone(),
+                                  **{k: v for k, v in kh.items() if k != "indicators"})
+    oracle.fused_multistep(args)
+    torch.cuda.synchronize()
+    assert torch.equal(ver.offsets.cpu(), ref.offsets)
+    assert torch.equal(ver.tokens.cpu(), ref.tokens)
+    if kw.get("decode_counts") is not None:
+        assert torch.equal(kw["decode_counts"].cpu(), kh["decode_counts"])
+    return ver, ref, kw, kh
+
+
+def _verify_logprobs_equal(ver, ref, ind, slots, margins):
+    sel, rsel = ver.logprobs.selected.reshape(-1), ref.logprobs.selected.reshape(-1)
+    for b, s in enumerate(slots):
+        if int(ind[s]) & 0x40:
+            continue
+        rows = slice(margins[b], margins[b] + int(ver.offsets[b]) + 1)
+        assert torch.equal(bits(sel[rows]), bits(rsel[rows]))
+
+
+@pytest.mark.parametrize("qdtype", [F32, BF16])
+def test_config3_varlen(dev, qdtype):
+    w = workloads.config3(dev, seed=8)
+    b = w["buffers"]
+    kw = buffer_kwargs(b, timestep=None)
+    ver, ref, kw, kh = run_multistep(w["flat_logits"], w["flat_tokens"], cu_seqlens=w["cu_seqlens"],
+                                     lookahead=w["gamma"], max_top_logprobs=20, update_counts=True,
+                                     return_logprobs=True, draft_probabilities=w["probabilities"].to(qdtype),
+                                     block_n=4096, **kw)
+    cu = w["cu_seqlens"].cpu().tolist()
+    _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(32)), cu[:-1])
+    assert int(ver.offsets.max()) >= 1  # some drafts accepted
+
+
+def test_config3_fixed_modular(dev):
+    from sonic_sampler_b200.interface import UnshardedFusedMultistep
+
+    w = workloads.config3(dev, seed=9, varlen=False)
+    b = w["buffers"]
+    ms = UnshardedFusedMultistep.initialize(128256, lookahead=w["gamma"], batch_size=32, max_top_logprobs=20)
+    ver = ms(w["logits"], w["tokens"], b, probabilities=w["probabilities"], logprobs=True)
+    kw = buffer_kwargs(b, timestep=None)
+    _, ref, _, _ = run_multistep(w["logits"], w["tokens"], lookahead=w["gamma"], max_top_logprobs=20,
+                                 return_logprobs=True, draft_probabilities=w["probabilities"],
+                                 block_n=ms.block_n, **kw)
+    assert torch.equal(ver.tokens.cpu(), ref.tokens)
+    assert torch.equal(ver.offsets.cpu(), ref.offsets)
+
+
+# ----------------------------------------------------------------------------------------
+# config 4: cross-vocab greedy drafting chain + greedy verification in one CUDA graph
+# ----------------------------------------------------------------------------------------
+
+
+def test_config4_graph_chain(dev):
+    from oracle import oracle
+    from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
+    from sonic_sampler_b200.interface.functional.multistep import prepare_multistep
+    from sonic_sampler_b200.interface.functional.singular import prepare_singular
+
+    w = workloads.config4(dev, seed=10)
+    b, gamma, d2t, sm = w["buffers"], w["gamma"], w["d2t"], w["slot_mapping"]
+    active = sm.numel()
+    drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
+    verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+    tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
+    # the verifier reads drafted tokens per request, the drafter per slot: use a slot-indexed
+    # token table for drafting and gather it for verification
+    slot_tokens = torch.zeros(b.top_k.numel(), gamma + 1, dtype=I32, device=dev)
+
+    def chain():
+        for t in range(gamma):
+            sel = drafter.drafting(w["draft_logits"][t], b, timestep=t, tokens=slot_tokens if t else None,
+                                   slot_mapping=sm, d2t_mapping=d2t, target_vocab=128256)
+            slot_tokens[sm.long(), t] = sel.tokens[:, 0]
+        tokens.copy_(slot_tokens[sm.long()])
+        return verifier(w["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
+
+    g = torch.cuda.CUDAGraph()
+    chain()  # warm-up outside capture
+    torch.cuda.synchronize()
+    slot_tokens.zero_()
+    with torch.cuda.graph(g):
+        ver = chain()
+    slot_tokens.zero_()
+    g.replay()
+    torch.cuda.synchronize()
+
+    # oracle replay of the same chain on the host
+    hb = b.to("cpu")
+    hst = torch.zeros_like(slot_tokens, device="cpu")
+    hsm, hd2t = sm.cpu(), d2t.cpu()
+    for t in range(gamma):
+        kw = buffer_kwargs(hb, timestep=t, draft=True)
+        ref, args = prepare_singular(w["draft_logits"][t].cpu(), lookahead=gamma, target_vocab=128256,
+                                     block_n=drafter.tuning(active)[2], slot_mapping=hsm, d2t_mapping=hd2t,
+                                     drafted_tokens=hst if t else None, **kw)
+        oracle.fused_singular(args)
+        hst[hsm.long(), t] = ref.tokens[:, 0]
+    htok = hst[hsm.long()].clone()
+    kw = buffer_kwargs(hb, timestep=None)
+    rver, args = prepare_multistep(w["target_logits"].cpu(), kw.pop("indicators"), htok, lookahead=gamma,
+                                   block_n=verifier.block_n, slot_mapping=hsm, output_tokens=htok, **kw)
+    oracle.fused_multistep(args)
+    assert torch.equal(slot_tokens.cpu(), hst)
+    assert torch.equal(ver.offsets.cpu(), rver.offsets)
+    assert torch.equal(ver.tokens.cpu(), rver.tokens)
+
+
+# ----------------------------------------------------------------------------------------
+# configs 1 and 5: bounded top-k and large-vocabulary Philox sampling
+# ----------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("dtype", [F32, BF16])
+def test_config1_topk(dev, dtype):
+    from oracle import oracle
+    from sonic_sampler_b200 import ops
+    from sonic_sampler_b200.interface import UnshardedBoundedTopK
+
+    w = workloads.config1(dev, seed=0)
+    x, k = w["logits"].to(dtype), w["k"]
+    topk = UnshardedBoundedTopK.initialize(32000, batch_size=8, k=k).clear()
+    values, indices = topk(x)
+    torch.cuda.synchronize()
+    vals = values.reshape(-1)[: 8 * k].view(8, k).cpu()
+    idx = indices.reshape(-1)[: 8 * k].view(8, k).cpu()
+    hv = torch.empty(8 * k, dtype=dtype)
+    hi = torch.empty(8 * k, dtype=I32)
+    oracle.bounded_topk(ops.topk_args(x.cpu(), vocab_size=32000, k=k, block_n=topk.block_n, values=hv, indices=hi))
+    assert torch.equal(idx, hi.view(8, k))
+    assert torch.equal(bits(vals), bits(hv.view(8, k)))
+    tv, ti = torch.topk(x.cpu().float(), k, dim=-1)
+    torch.testing.assert_close(vals.float(), tv, rtol=0, atol=0)
+
+
+def test_config5_philox_full(dev):
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.singular import fused_singular, prepare_singular
+
+    w = workloads.config5(dev, seed=1)
+    x = w["logits"]
+    kw = dict(indicators=w["indicators"], top_k=w["top_k"], top_p=w["top_p"], block_n=4096,
+              philox_seed=w["philox_seed"], philox_offset=17, return_logprobs=True, logprobs_dtype=F32)
+    sel = fused_singular(x, **kw)
+    torch.cuda.synchronize()
+    rows = torch.arange(0, 1024, 16)  # oracle on a row sample
+    kh = host(kw)
+    kh["slot_mapping"] = rows.to(I32)
+    ref, args = prepare_singular(x[rows].cpu(), **kh)
+    oracle.fused_singular(args)
+    assert torch.equal(sel.tokens[rows].cpu(), ref.tokens)
+    assert torch.equal(bits(sel.logprobs.selected[rows]), bits(ref.logprobs.selected))
+
+
+def test_philox_chi_squared(dev):
+    """Counter-based noise: the empirical token distribution over many offsets matches the
+    truncated softmax (top-k 8) of the row."""
+    from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+    vocab, draws = 4096, 4096
+    g = torch.Generator().manual_seed(3)
+    row = torch.full((vocab,), -30.0)
+    row[torch.randperm(vocab, generator=g)[:8]] = torch.tensor([2.0, 1.5, 1.0, 0.5, 0.0, -0.5, -1.0, -1.5])
+    x = row.to(BF16).to(dev).expand(draws, vocab).contiguous()
+    ind = torch.full((draws,), 0x80, dtype=torch.uint16, device=dev)
+    top_k = torch.full((draws,), 8, dtype=I32, device=dev)
+    # one row per slot, distinct slots -> independent counters
+    sel = fused_singular(x, ind, top_k=top_k, block_n=1024, philox_seed=1234, philox_offset=0)
+    toks = sel.tokens.flatten().cpu()
+    support = torch.topk(row, 8).indices
+    assert bool(torch.isin(toks, support).all())
+    p = torch.softmax(row.to(BF16).float()[support], 0)
+    counts = torch.stack([(toks == t).sum() for t in support]).double()
+    expected = p.double() * draws
+    chi2 = float(((counts - expected) ** 2 / expected).sum())
+    # chi-squared with 7 degrees of freedom: P(chi2 > 24.32) = 0.001
+    assert chi2 < 24.32, (chi2, counts.tolist(), expected.tolist())
+
+
+# ----------------------------------------------------------------------------------------
+# edge cases
+# ----------------------------------------------------------------------------------------
+
+
+def _params(dev, slots, vocab, seed, **kw):
+    b = workloads.sampling_buffers(slots, 1, vocab, dev, seed, workloads.config2_params(slots, seed + 1), **kw)
+    return b
+
+
+@pytest.mark.parametrize("vocab", [130, 1000, 32001, 70001])
+def test_ragged_vocab_scalar_path(dev, vocab):
+    """Vocab sizes that are not multiples of 8 (scalar loads, ragged last split)."""
+    b = _params(dev, 6, vocab, seed=vocab, top_logprobs=3)
+    x = workloads.peaked_logits(6, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=vocab)
+    sel, ref, kw, kh = run_singular(x, block_n=256, update_counts=True, return_logprobs=True, max_top_logprobs=4,
+                                    **buffer_kwargs(b))
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_misaligned_logits_view(dev):
+    """A logits view starting one element in (not 16-byte aligned) takes the scalar path."""
+    b = _params(dev, 8, 8191, seed=2)
+    base = workloads.peaked_logits(8, 8192, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=2)
+    x = base[:, 1:]
+    sel, ref, kw, kh = run_singular(x, block_n=1024, return_logprobs=True, **buffer_kwargs(b))
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_fully_masked_rows(dev):
+    """Rows whose grammar masks every token: every logit is -inf."""
+    b = _params(dev, 4, 4096, seed=3, grammar_density=0.0)
+    x = workloads.peaked_logits(4, 4096, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=3)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, return_logprobs=True, **buffer_kwargs(b))
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_greedy_tie_rule_per_block_n(dev):
+    """Equal maxima at offset 100 of tile 0 and offset 5 of tile 1: the reference's tile rule
+    picks the smaller in-tile offset, so the answer depends on block_n."""
+    from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+    x = torch.zeros(2, 8192, dtype=BF16, device=dev)
+    x[:, 100] = 9.0
+    x[0, 1024 + 5] = 9.0
+    x[1, 4096 + 5] = 9.0
+    ind = torch.full((2,), 0x40, dtype=torch.uint16, device=dev)
+    assert fused_singular(x, ind, block_n=1024).tokens.flatten().tolist() == [1029, 4101]
+    assert fused_singular(x, ind, block_n=4096).tokens.flatten().tolist() == [100, 4101]
+
+
+def test_slot_mapping_int64_d2t_int32(dev):
+    vd, vt, slots = 5000, 9000, 12
+    b = _params(dev, slots, vt, seed=4, top_logprobs=2)
+    x = workloads.peaked_logits(7, vd, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=4)
+    d2t = torch.randperm(vt, generator=torch.Generator().manual_seed(4))[:vd].to(I32).to(dev)
+    sm = torch.tensor([11, 3, 0, 7, 5, 9, 1], dtype=torch.int64, device=dev)
+    probs = torch.zeros(slots, vt, dtype=BF16, device=dev)
+    kw = buffer_kwargs(b)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, slot_mapping=sm, d2t_mapping=d2t, target_vocab=vt,
+                                    return_probabilities=True, draft_probabilities=probs, update_counts=True,
+                                    is_prefill=True, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_top_logprobs_request_above_capacity_is_clamped(dev):
+    b = _params(dev, 4, 4096, seed=5, top_logprobs=9)
+    x = workloads.peaked_logits(4, 4096, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=5)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, return_logprobs=True, max_top_logprobs=4, **buffer_kwargs(b))
+    assert torch.equal(sel.tokens.cpu(), ref.tokens)
+    assert torch.equal(bits(sel.logprobs.top_k.logprobs), bits(ref.logprobs.top_k.logprobs))
+    assert torch.equal(sel.logprobs.top_k.tokens.cpu(), ref.logprobs.top_k.tokens)
+
+
+def test_large_batch_many_rows(dev):
+    """More rows than SMs x resident CTAs (several waves, one split per row)."""
+    b = _params(dev, 2048, 4096, seed=6)
+    x = workloads.peaked_logits(2048, 4096, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=6)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, update_counts=True, **buffer_kwargs(b))
+    assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_empty_batch_is_a_no_op(dev):
+    from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+    x = torch.empty(0, 4096, dtype=BF16, device=dev)
+    sel = fused_singular(x, torch.zeros(4, dtype=torch.uint16, device=dev),
+                         gumbel_noise=torch.zeros(4, 4096, dtype=BF16, device=dev))
+    assert sel.tokens.shape == (0, 1)
+
+
+def test_multistep_greedy_mixed_bf16_logprobs(dev):
+    """Greedy and stochastic requests in one multistep batch, slot mapping, bf16 outputs."""
+    gamma, vocab, batch, slots = 3, 32000, 6, 9
+    b = workloads.sampling_buffers(slots, gamma + 1, vocab, dev, 12, workloads.config2_params(slots, 13),
+                                   top_logprobs=3)
+    ind = b.flags.target.cpu().to(torch.int32)
+    ind[::3] = (ind[::3] & 0x3F) | 0x40
+    b.flags.packed[:, 0] = ind.to(torch.uint16).to(dev)
+    sm = torch.tensor([8, 0, 3, 4, 6, 1], dtype=I32, device=dev)
+    x = workloads.peaked_logits(batch * (gamma + 1), vocab, sigma=3.0, peaks=4, lift=12.0, device=dev,
+                                seed=14).view(batch, gamma + 1, vocab)
+    tokens = x.float().argmax(-1).to(I32).contiguous()
+    tokens[1, 2] = (tokens[1, 2] + 1) % vocab
+    kw = buffer_kwargs(b, timestep=None)
+    ver, ref, kw, kh = run_multistep(x, tokens, lookahead=gamma, block_n=2048, slot_mapping=sm,
+                                     update_counts=True, return_logprobs=True, max_top_logprobs=3, **kw)
+    margins = [i * (gamma + 1) for i in range(batch)]
+    _verify_logprobs_equal(ver, ref, kh["indicators"], sm.cpu().tolist(), margins)
