@@ -105,8 +105,8 @@ def prepare_singular(
     Works for host tensors too (no workspace is attached then)."""
     validate_count_update(update_counts, decode_counts)
     if world_size > 1:
-        raise ValueError("vocab-sharded singular sampling goes through "
-                         "sonic_sampler_b200.parallel.vocab_sharded_singular (one all-gather)")
+        raise ValueError("vocab-sharded singular sampling is not available in this library yet; "
+                         "shard requests by rows")
 
     batch_size, vocab_size = logits.shape
     vocab_size = min(vocab_size, local_vocab or vocab_size)
