@@ -221,6 +221,21 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* args, void* stream);
 sonic_status sonic_fused_multistep(const SonicMultistepArgs* args, void* stream);
 sonic_status sonic_bounded_topk(const SonicTopKArgs* args, void* stream);
 
+/* sonic_fused_singular for callers that cannot allocate device memory (an engine whose KV
+ * cache already holds all free HBM, a cgo / JNI binding without the framework's allocator,
+ * a loop that cannot afford cudaMalloc's possible device synchronisation). No counterpart
+ * in the reference: it is an addition of this library.
+ *
+ * args->workspace and args->workspace_bytes are ignored; the scratch is a fixed 4 MiB device
+ * array inside this library, held by every GPU that loads it until the process exits.
+ * Calls whose sonic_fused_singular_workspace_size() exceeds 4 MiB fail with
+ * SONIC_ERR_WORKSPACE. The first call on a device looks up the array's device address (with
+ * that device current); make that first call before any stream capture. Each call clears
+ * the array's tickets with cudaMemsetAsync on `stream` and allocates nothing. All calls
+ * share the one array: calls that may overlap on the GPU (other streams, other host threads
+ * on the same device) race and must be serialised by the caller. */
+sonic_status sonic_fused_singular_static(const SonicSingularArgs* args, void* stream);
+
 /* ABI version (SONIC_B200_ABI_VERSION) the library was built with. */
 int32_t sonic_abi_version(void);
 /* Message of the calling thread's last failed call ("" when none). */

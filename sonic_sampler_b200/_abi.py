@@ -172,6 +172,7 @@ EXPORTED_SYMBOLS = (
     "sonic_fused_singular",
     "sonic_fused_multistep",
     "sonic_bounded_topk",
+    "sonic_fused_singular_static",
     "sonic_abi_version",
     "sonic_last_error",
 )
@@ -193,6 +194,7 @@ def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
         ("sonic_fused_singular", SingularArgs),
         ("sonic_fused_multistep", MultistepArgs),
         ("sonic_bounded_topk", TopKArgs),
+        ("sonic_fused_singular_static", SingularArgs),
     ):
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(argt), _vp]

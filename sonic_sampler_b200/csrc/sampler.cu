@@ -26,6 +26,7 @@
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <string>
 #include <type_traits>
 
@@ -2229,3 +2230,67 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------------------
+// singular call without a caller workspace
+//
+// For hosts that cannot allocate device memory for this library: a serving engine that has
+// already handed all free HBM to its KV cache, a foreign-language binding (cgo, JNI) with no
+// access to the framework's caching allocator, or a latency-critical loop where a
+// cudaMalloc, which may synchronise the device, is not acceptable. The scratch lives in a
+// fixed device array instead; every GPU that loads this library holds it until the process
+// exits.
+// ---------------------------------------------------------------------------------------
+
+namespace sonic {
+
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+constexpr int kMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+
+// Device address of g_static_scratch on the current device. In host code the array's name
+// is only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per
+// device, with that device current.
+static sonic_status static_scratch(void** out) {
+  static std::mutex mu;
+  static void* addr[kMaxDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(SONIC_ERR_UNSUPPORTED, "device ordinal beyond the static scratch table");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_static_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(SONIC_ERR_CUDA, std::string("cudaGetSymbolAddress(static scratch): ") + cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return SONIC_OK;
+}
+
+}  // namespace sonic
+
+extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, void* stream) {
+  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
+  if (a->rows == 0) return SONIC_OK;
+  const size_t need = sonic_fused_singular_workspace_size(a);
+  if (need > kStaticScratchBytes)
+    return fail(SONIC_ERR_WORKSPACE, "sonic_fused_singular_static: this call needs " + std::to_string(need) +
+                                         " bytes of scratch, more than the " + std::to_string(kStaticScratchBytes) +
+                                         "-byte static scratch; use sonic_fused_singular with a workspace");
+  void* base = nullptr;
+  if (sonic_status s = static_scratch(&base)) return s;
+  // the tickets and the error word start at zero; the candidate lists are written before use
+  const Plan p = singular_plan(a->rows, a->vocab_size);
+  const Workspace ws = carve(base, a->rows, a->rows, p.splits);
+  const size_t off = (size_t)((char*)ws.tickets - (char*)base);
+  const cudaError_t e = cudaMemsetAsync(ws.tickets, 0, need - off, (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("sonic_fused_singular_static: ") + cudaGetErrorString(e));
+  SonicSingularArgs b = *a;
+  b.workspace = base;
+  b.workspace_bytes = kStaticScratchBytes;
+  return sonic_fused_singular(&b, stream);
+}
