@@ -536,10 +536,12 @@ __device__ __forceinline__ MaskParams load_mask_params(const SonicSamplingParams
   return m;
 }
 
-// cumulative_masking (ops/base.py:95-129) on the sorted top-128 held 4 per lane.
-__device__ __forceinline__ void warp_masking(const MaskParams& M, uint32_t ind, float (&v)[4], float maximum,
-                                             int lane) {
+// cumulative_masking (ops/base.py:95-129) on the sorted top-128 held 4 per lane. When top-p
+// runs, e receives exp(v - maximum) of the values it saw and the call returns true.
+__device__ __forceinline__ bool warp_masking(const MaskParams& M, uint32_t ind, float (&v)[4], float maximum,
+                                             int lane, float (&e)[4]) {
   const float ninf = __int_as_float(0xff800000);
+  bool have_e = false;
   if ((ind & 0x80) && M.has_k) {
     const int32_t k = M.top_k;
 #pragma unroll
@@ -547,7 +549,8 @@ __device__ __forceinline__ void warp_masking(const MaskParams& M, uint32_t ind, 
       if (!(4 * lane + j < k)) v[j] = ninf;
   }
   if ((ind & 0x100) && M.has_p) {
-    float e[4], lad[4];
+    float lad[4];
+    have_e = true;
 #pragma unroll
     for (int j = 0; j < 4; ++j) e[j] = dexp(__fsub_rn(v[j], maximum));
     warp_ladder128(e, lad, lane);
@@ -563,15 +566,19 @@ __device__ __forceinline__ void warp_masking(const MaskParams& M, uint32_t ind, 
     for (int j = 0; j < 4; ++j)
       if (!(v[j] >= pivot)) v[j] = ninf;
   }
+  return have_e;
 }
 
-// log_softmax (ops/base.py:66-72) of 128 values held 4 per lane.
-__device__ __forceinline__ void warp_log_softmax(const float (&v)[4], float maximum, float (&ls)[4]) {
+// log_softmax (ops/base.py:66-72) of 128 values held 4 per lane. With have_e, e already
+// holds exp(v - maximum) for every value that is not -inf (from the top-p mask); it is
+// reused instead of recomputed (exp(-inf) is 0, the same bits as recomputing).
+__device__ __forceinline__ void warp_log_softmax(const float (&v)[4], float maximum, float (&ls)[4],
+                                                 bool have_e = false, const float* e_in = nullptr) {
   float sc[4], e[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     sc[j] = __fsub_rn(v[j], maximum);
-    e[j] = dexp(sc[j]);
+    e[j] = have_e ? (v[j] == __int_as_float(0xff800000) ? 0.0f : e_in[j]) : dexp(sc[j]);
   }
   const float lse = dlog(warp_sum128(e));
 #pragma unroll
@@ -672,8 +679,12 @@ __device__ __forceinline__ void wtk_push(WarpTopK<K>& w, K* q, const K (&key)[VP
 // list (both in shared memory); returns the value of the 128th kept key (-inf while fewer
 // than 128 are kept). Not inlined: it runs rarely and is large, and one copy keeps the
 // streaming loop inside the instruction cache.
+// A non-zero `tq` marks queues that hold pre-temperature keys (the fast path of stochastic
+// rows): their values are tempered (temper(v, 1, tfast, t, rt)) before the sort, so the list
+// holds final keys and ties between final values fall back to the lowest column.
 template <typename K>
-__device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane) {
+__device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane, int tq, int tfast, float t,
+                                           float rt) {
   __syncwarp();
   K l[4];
 #pragma unroll
@@ -684,6 +695,11 @@ __device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane
     for (int j = 0; j < 4; ++j) {
       const int i = base + 4 * lane + j;
       k[j] = i < qn ? q[i] : (K)0;
+      if (sizeof(K) == 4 && tq && k[j]) {
+        const uint32_t u = (uint32_t)k[j];
+        const float f = temper(bf2f((uint16_t)dec16(u >> 16)), true, tfast != 0, t, rt);
+        k[j] = (K)((enc16(f2bf(f)) << 16) | (u & 0xffffu));
+      }
     }
     warp_sort128_desc(k, lane);
     warp_merge128_desc(l, k, lane);
@@ -696,10 +712,11 @@ __device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane
 }
 
 template <typename K>
-__device__ __forceinline__ float wtk_absorb(WarpTopK<K>& w, const K* q, int lane) {
-  const float t = absorb_queue<K>(w.list, q, w.qn, lane);
+__device__ __forceinline__ float wtk_absorb(WarpTopK<K>& w, const K* q, int lane, bool tq = false,
+                                            bool tfast = false, float t = 1.0f, float rt = 1.0f) {
+  const float r = absorb_queue<K>(w.list, q, w.qn, lane, tq, tfast, t, rt);
   w.qn = 0;
-  return t;
+  return r;
 }
 
 // Merge the NW warp lists (shared memory, overwritten) into warp 0's registers with a
@@ -748,7 +765,10 @@ __device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* x
     for (int t = 1; t < PER; ++t)
       if (warp + t * NW < splits) warp_merge128_desc(acc, pre[t], lane);
   }
-  for (int width = NW / 2; width >= 1; width >>= 1) {
+  // tree over the warps that hold lists (splits is uniform over the CTA)
+  int width = 1;
+  while (2 * width < min(splits, NW)) width *= 2;
+  for (; width >= 1 && splits > 1; width >>= 1) {
     if (warp >= width && warp < 2 * width)
 #pragma unroll
       for (int j = 0; j < 4; ++j) xchg[(warp - width) * kMaxK + 4 * lane + j] = acc[j];
@@ -759,30 +779,31 @@ __device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* x
       for (int j = 0; j < 4; ++j) b[j] = xchg[warp * kMaxK + 4 * lane + j];
       warp_merge128_desc(acc, b, lane);
     }
-    __syncthreads();
+    if (width > 1) __syncthreads();
   }
 #pragma unroll
   for (int j = 0; j < 4; ++j) out[j] = acc[j];
 }
 
 // ---------------------------------------------------------------------------------------
-// single-row streaming: warp-private groups of 256 columns (8 per lane). Each warp owns a
-// ring of bulk-copy stages (one group each) that its lane 0 refills as soon as the warp
-// has consumed a stage, so several groups per warp are always in flight and warps never
-// wait for one another until the split's lists are folded. Groups the ring cannot take
-// (a ragged tail, unaligned or gathered rows) use direct loads.
+// single-row streaming: groups of 256 columns (8 per lane) owned by one warp each. Full
+// 2048-column chunks of a split arrive through a CTA-wide ring of bulk-copy stages (one
+// chunk, 5 large copies, per stage); warp w consumes the w-th 256 columns of each chunk and
+// the last warp to finish a stage refills it, so warps never wait for one another within
+// the ring's depth. Groups the ring cannot take (a ragged tail, unaligned or gathered rows)
+// use direct loads.
 // ---------------------------------------------------------------------------------------
 
 constexpr int GROUP = VPT * 32;  // columns of one warp group
 constexpr int PF_GROUPS = 4;     // L2 prefetch distance of direct loads, in groups of one warp
-constexpr int WST = 3;           // bulk-copy stages per warp
-// stage layout (bytes) of one group: logits, decode counts, context counts, bias, grammar
-constexpr int WS_X = 0;
-constexpr int WS_D = WS_X + GROUP * 2;
-constexpr int WS_C = WS_D + GROUP * 4;
-constexpr int WS_B = WS_C + GROUP * 4;
-constexpr int WS_G = WS_B + GROUP * 2;
-constexpr int WS_BYTES = WS_G + GROUP / 8;  // 3104
+// bulk-copy stage layout (bytes) of one 2048-column chunk: logits, decode counts, context
+// counts, bias, grammar words
+constexpr int SG_X = 0;
+constexpr int SG_D = SG_X + CH * 2;
+constexpr int SG_C = SG_D + CH * 4;
+constexpr int SG_B = SG_C + CH * 4;
+constexpr int SG_G = SG_B + CH * 2;
+constexpr int SG_STAGE = SG_G + CH / 8;  // 24832
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -791,33 +812,36 @@ __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
 // Smallest bf16 v (finite or +inf, as a bf16 pair) whose final value is >= thr: a guess
 // from thr * temperature, corrected a few steps along the order-preserving encoding (the
 // final value is monotone in v); binary search when the guess is far off.
-__device__ __noinline__ uint32_t vmin_pair(float thr, bool on, bool fast, float t, float rt) {
-  constexpr uint32_t kLo = 0x0080u, kHi = 0xff80u;  // enc of -max finite .. enc of +inf
+constexpr uint32_t kEncLo = 0x0080u, kEncHi = 0xff80u;  // enc of -max finite .. enc of +inf
+
+__device__ __noinline__ uint32_t vmin_search(float thr, bool on, bool fast, float t, float rt) {
+  uint32_t lo = kEncLo, hi = kEncHi;
+  while (lo < hi) {
+    const uint32_t mid = (lo + hi) >> 1;
+    if (temper(bf2f((uint16_t)dec16(mid)), on, fast, t, rt) >= thr) hi = mid;
+    else lo = mid + 1;
+  }
+  return lo;
+}
+
+__device__ __forceinline__ uint32_t vmin_pair(float thr, bool on, bool fast, float t, float rt) {
   auto ok = [&](uint32_t e) { return temper(bf2f((uint16_t)dec16(e)), on, fast, t, rt) >= thr; };
   const float guess = on ? __fmul_rn(thr, t) : thr;
-  uint32_t e = umin(umax(enc16(f2bf(guess)), kLo), kHi);
+  uint32_t e = umin(umax(enc16(f2bf(guess)), kEncLo), kEncHi);
   bool done = false;
   if (ok(e)) {
     for (int i = 0; i < 4 && !done; ++i) {
-      if (e == kLo || !ok(e - 1)) done = true;
+      if (e == kEncLo || !ok(e - 1)) done = true;
       else --e;
     }
   } else {
     for (int i = 0; i < 4 && !done; ++i) {
-      if (e == kHi) break;
+      if (e == kEncHi) break;
       ++e;
       if (ok(e)) done = true;
     }
   }
-  if (!done) {
-    uint32_t lo = kLo, hi = kHi;
-    while (lo < hi) {
-      const uint32_t mid = (lo + hi) >> 1;
-      if (ok(mid)) hi = mid;
-      else lo = mid + 1;
-    }
-    e = lo;
-  }
+  if (!done) e = vmin_search(thr, on, fast, t, rt);
   const uint32_t h = dec16(e);
   return h | (h << 16);
 }
@@ -833,12 +857,13 @@ struct RowSmem {
   K lists[NW][kMaxK];
   unsigned long long cut;  // packed CTA cut, see pack_cut
   float v16[NW];           // each warp's 16th kept key value (-inf while it keeps fewer)
-  float vlm[NW];           // each warp's 16th largest lane maximum (see lane_max_cut)
+  float vlm[NW];           // each warp's 16th largest lane maximum (see lane_max_publish)
   MaskParams mp;           // the slot's masking parameters (selection epilogue)
   int flag;
   unsigned long long best;
   int32_t toks[SONIC_MAX_LOOKAHEAD + 1];
-  uint64_t bars[NW][WST];
+  uint64_t bars[STAGES];  // bulk-copy stage filled
+  int rel[STAGES];        // warps done with the stage
 };
 
 // After an absorb: the warp's new threshold candidates are its own 128th key value and the
@@ -869,15 +894,19 @@ __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v, int lane) {
   return v;
 }
 
-// Each lane's largest pushed key belongs to a distinct column, so the 16th largest lane
-// maximum of every warp bounds 8 x 16 = 128 distinct keys of the split from below: the
-// smallest of those over the warps is a valid cut. Warp-wide; returns that cut (-inf while
-// some warp has not published).
-__device__ __forceinline__ float lane_max_cut(uint32_t lmax, float* vlm, int warp, int lane) {
+// Each lane's largest key belongs to a distinct column, so the 16th largest lane maximum of
+// every warp bounds 8 x 16 = 128 distinct keys of the split from below: the smallest of
+// those over the warps is a valid cut. lane_max_publish stores a warp's 16th largest lane
+// maximum (as a final value); lane_max_min reads the smallest over the warps.
+template <typename F>
+__device__ __forceinline__ void lane_max_publish(uint32_t lmax, float* vlm, int warp, int lane, F final_of) {
   const uint32_t k16 = __shfl_sync(kFull, warp_sort32_desc(lmax, lane), 15);
-  if (lane == 0) reinterpret_cast<volatile float*>(vlm)[warp] = k16 ? key_value<uint32_t>(k16) : __int_as_float(0xff800000);
-  __syncwarp();
-  float m = lane < NW ? reinterpret_cast<volatile float*>(vlm)[lane] : __int_as_float(0x7f800000);
+  if (lane == 0)
+    reinterpret_cast<volatile float*>(vlm)[warp] = k16 ? final_of(key_value<uint32_t>(k16)) : __int_as_float(0xff800000);
+}
+
+__device__ __forceinline__ float lane_max_min(const float* vlm, int lane) {
+  float m = lane < NW ? reinterpret_cast<const volatile float*>(vlm)[lane] : __int_as_float(0x7f800000);
 #pragma unroll
   for (int d = 4; d >= 1; d >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, d));
   return __shfl_sync(kFull, m, 0);
@@ -942,24 +971,51 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const bool greedy = (ind & 0x40) != 0;
   const int ntok = (a.drafted_tokens && rc.nd.dec) ? a.lookahead : 0;
   if (tid < ntok) st.toks[tid] = a.drafted_tokens[slot * a.drafted_stride + tid];
+  // streams of the bulk-copy ring (see below)
+  const int64_t shard = a.shard_offset;
+  const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
+  const uint32_t* grow = rc.nd.g ? P.grammar + slot * P.grammar_stride : nullptr;
+  const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
+  const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
+  const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
+  const uint32_t tx = CH * 2 + (drow ? CH * 4 : 0) + (crow ? CH * 4 : 0) + (brow ? CH * 2 : 0) + (grow ? CH / 8 : 0);
+  auto issue_chunk = [&](int i) {  // one thread
+    unsigned char* sp = smem_ring + (i % STAGES) * SG_STAGE;
+    uint64_t* bar = &st.bars[i % STAGES];
+    const int64_t cc = c0 + (int64_t)i * CH;
+    mbar_expect_tx(bar, tx);
+    bulk_load(sp + SG_X, xrow + cc, CH * 2, bar);
+    if (drow) bulk_load(sp + SG_D, drow + cc + shard, CH * 4, bar);
+    if (crow) bulk_load(sp + SG_C, crow + cc + shard, CH * 4, bar);
+    if (brow) bulk_load(sp + SG_B, brow + cc + shard, CH * 2, bar);
+    if (grow) bulk_load(sp + SG_G, grow + (cc + shard) / 32, CH / 8, bar);
+  };
   if (tid == 0) {
     st.best = 0ull;
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
+    if (MODE == kTma) {
+      for (int i = 0; i < STAGES; ++i) {
+        mbar_init(&st.bars[i], 1);
+        st.rel[i] = 0;
+      }
+      mbar_fence_init();
+      const int nch = (int)((c1 - c0) / CH);
+      for (int i = 0; i < min(nch, STAGES); ++i) issue_chunk(i);
+    }
   }
   __syncthreads();
 
-  const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
-  const int64_t shard = a.shard_offset;
   uint32_t* q = st.queue[warp];
   WarpTopK<uint32_t> w;
   wtk_init(w, st.lists[warp], kFiniteFloor, lane);  // the first wtk_adopt takes the fast-path pair from st.cut
   uint64_t best = 0;
-  uint32_t lmax = 0;  // largest key this lane has pushed (fast path)
+  bool tq = rc.fast && rc.nd.temp;  // fast-path queues hold pre-temperature keys
+  auto final_of = [&](float v) { return final_value(v, rc); };
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
-      const float t = absorbed_cut(w, wtk_absorb(w, q, lane), st.v16, warp, lane);
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp), st.v16, warp, lane);
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
     }
   };
@@ -996,7 +1052,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   // penalties only where a count is nonzero (they are the identity elsewhere). Where the
   // penalties cannot raise a logit (rc.decr, counts >= 0) the candidate test runs on the
   // unpenalised value first and only candidates are penalised and tested again.
-  auto fast_group = [&](const Raw8& raw, int64_t c, int nvalid) {
+  auto fast_group = [&](const Raw8& raw, int64_t c, int nvalid) -> int {
     uint32_t x[4] = {raw.x[0], raw.x[1], raw.x[2], raw.x[3]};
     // columns whose counts (or drafted tokens) are nonzero; computed only when needed
     auto need_bits = [&]() {
@@ -1040,7 +1096,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
     uint32_t m = ge_mask8(y, w.vmin2) & raw.g;
     if (nvalid < VPT) m &= (1u << max(nvalid, 0)) - 1u;
-    if (!__any_sync(kFull, m)) return;
+    if (!__any_sync(kFull, m)) return 0;
     // candidates of the unpenalised test: penalise those with nonzero counts, test again
     if (__any_sync(kFull, counted && m)) {
       const uint32_t late = (counted && m) ? (m & need_bits()) : 0u;
@@ -1059,26 +1115,19 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       const int j = __ffs(m) - 1;
       m &= m - 1;
       const uint32_t word = select4(y, j >> 1);
-      const float fv = final_value(bf2f((uint16_t)((j & 1) ? (word >> 16) : (word & 0xffffu))), rc);
-      const uint32_t key = (enc16(f2bf(fv)) << 16) | (base - (uint32_t)j);
+      const uint32_t key = (enc16((j & 1) ? (word >> 16) : (word & 0xffffu)) << 16) | (base - (uint32_t)j);
       q[pos++] = key;
-      lmax = umax(lmax, key);
     }
     w.qn += total;
+    return total;
   };
 
   auto process_group = [&](Raw8& raw, int64_t c, int nvalid, int k) {
     if (!greedy) wtk_adopt(w, &st.cut, lane);
-    if (rc.fast) {
+    if (rc.fast)
       fast_group(raw, c, nvalid);
-      if (k < 3) {
-        // bootstrap the cut from the lane maxima of the first groups
-        const float t = lane_max_cut(lmax, st.vlm, warp, lane);
-        if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
-      }
-    } else {
+    else
       exact_group(raw, c, nvalid);
-    }
     if (!greedy) absorb_if_full();
   };
 
@@ -1088,54 +1137,51 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   auto gvalid = [&](int g) { return (int)max((int64_t)0, min((int64_t)VPT, c1 - gcol(g))); };
   constexpr int DM = MODE == kTma ? kVec : MODE;  // direct loads
 
-  // full groups go through this warp's bulk-copy ring: its k-th group uses stage k % WST
-  const int nfull = MODE == kTma ? (int)((c1 - c0) / GROUP) : 0;
-  const int kfull = nfull > warp ? (nfull - warp + NW - 1) / NW : 0;
-  unsigned char* ring = smem_ring + (size_t)warp * WST * WS_BYTES;
-  const uint32_t* grow = rc.nd.g ? P.grammar + slot * P.grammar_stride : nullptr;
-  const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
-  const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
-  const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
-  const uint32_t tx =
-      GROUP * 2 + (drow ? GROUP * 4 : 0) + (crow ? GROUP * 4 : 0) + (brow ? GROUP * 2 : 0) + (grow ? GROUP / 8 : 0);
-  // lane i < 5 issues stream i (logits, decode counts, context counts, bias, grammar)
-  const unsigned char* sbase = nullptr;
-  int64_t sadd = 0;
-  int ssh = 0, sdsh = 0, soff = 0;
-  uint32_t sbytes = 0;
-  if (lane == 0) { sbase = (const unsigned char*)xrow; ssh = 1; soff = WS_X; sbytes = GROUP * 2; }
-  if (lane == 1 && drow) { sbase = (const unsigned char*)drow; sadd = shard; ssh = 2; soff = WS_D; sbytes = GROUP * 4; }
-  if (lane == 2 && crow) { sbase = (const unsigned char*)crow; sadd = shard; ssh = 2; soff = WS_C; sbytes = GROUP * 4; }
-  if (lane == 3 && brow) { sbase = (const unsigned char*)brow; sadd = shard; ssh = 1; soff = WS_B; sbytes = GROUP * 2; }
-  if (lane == 4 && grow) { sbase = (const unsigned char*)grow; sadd = shard; sdsh = 3; soff = WS_G; sbytes = GROUP / 8; }
-  auto issue = [&](int k) {  // warp-wide
-    uint64_t* bar = &st.bars[warp][k % WST];
-    if (lane == 0) mbar_expect_tx(bar, tx);
-    __syncwarp();
-    if (sbase) {
-      const int64_t cc = c0 + (int64_t)(warp + k * NW) * GROUP + sadd;
-      bulk_load(ring + (k % WST) * WS_BYTES + soff, sbase + ((cc << ssh) >> sdsh), sbytes, bar);
-    }
-  };
-  if (kfull > 0) {
-    if (lane == 0) {
-      for (int i = 0; i < WST; ++i) mbar_init(&st.bars[warp][i], 1);
-      mbar_fence_init();
-    }
-    __syncwarp();
-    for (int k = 0; k < min(kfull, WST); ++k) issue(k);
-  }
-
+  // chunk k (full 2048-column chunks only) is group k * NW + warp of every warp
+  const int nchunks = MODE == kTma ? (int)((c1 - c0) / CH) : 0;
   bool werr = false;
+  if (MODE == kTma && rc.fast && !greedy && nchunks > 0 && ntok == 0) {
+    // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
+    // columns whose counts are zero (their value needs no penalty), bound 128 distinct keys.
+    if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+    const uint4 xq = *reinterpret_cast<const uint4*>(smem_ring + SG_X + warp * (GROUP * 2) + lane * 16);
+    uint32_t y[4] = {xq.x, xq.y, xq.z, xq.w};
+    if (brow) {
+      const uint4 bq = *reinterpret_cast<const uint4*>(smem_ring + SG_B + warp * (GROUP * 2) + lane * 16);
+      y[0] = bf2_add(y[0], bq.x);
+      y[1] = bf2_add(y[1], bq.y);
+      y[2] = bf2_add(y[2], bq.z);
+      y[3] = bf2_add(y[3], bq.w);
+    }
+    uint32_t ok = grow ? smem_ring[SG_G + warp * (GROUP / 8) + lane] : 0xffu;
+    if (drow) {
+      const int32_t* dp = reinterpret_cast<const int32_t*>(smem_ring + SG_D + warp * (GROUP * 4)) + 8 * lane;
+      const int32_t* cp = reinterpret_cast<const int32_t*>(smem_ring + SG_C + warp * (GROUP * 4)) + 8 * lane;
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        if ((dp[j] | (crow ? cp[j] : 0)) != 0) ok &= ~(1u << j);
+    }
+    const uint32_t base = (uint32_t)(0xffff - (int)(gcol(warp) - c0));
+    uint32_t lm = 0;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const uint32_t h = half_of(y, j);
+      if (((ok >> j) & 1u) && (h & 0x7fffu) <= 0x7f80u) lm = umax(lm, (enc16(h) << 16) | (base - (uint32_t)j));
+    }
+    lane_max_publish(lm, st.vlm, warp, lane, final_of);
+    __syncthreads();
+    const float t = lane_max_min(st.vlm, lane);
+    if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
+  }
   for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     Raw8 raw;
-    const bool staged = k < kfull;
+    const bool staged = k < nchunks;
     if (staged) {
-      if (!mbar_wait_bounded(&st.bars[warp][k % WST], (uint32_t)(k / WST) & 1u, WAIT_LIMIT)) werr = true;
-      const unsigned char* sp = ring + (k % WST) * WS_BYTES;
-      const uint4 xq = *reinterpret_cast<const uint4*>(sp + WS_X + lane * 16);
+      if (!mbar_wait_bounded(&st.bars[k % STAGES], (uint32_t)(k / STAGES) & 1u, WAIT_LIMIT)) werr = true;
+      const unsigned char* sp = smem_ring + (k % STAGES) * SG_STAGE;
+      const uint4 xq = *reinterpret_cast<const uint4*>(sp + SG_X + warp * (GROUP * 2) + lane * 16);
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) raw.d[j] = raw.c[j] = 0;
@@ -1143,30 +1189,42 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       for (int p = 0; p < 4; ++p) raw.b[p] = 0;
       raw.g = 0xffu;
       if (drow) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_D + lane * 32);
-        const uint4 v = *reinterpret_cast<const uint4*>(sp + WS_D + lane * 32 + 16);
+        const unsigned char* dp = sp + SG_D + warp * (GROUP * 4) + lane * 32;
+        const uint4 u = *reinterpret_cast<const uint4*>(dp);
+        const uint4 v = *reinterpret_cast<const uint4*>(dp + 16);
         raw.d[0] = u.x; raw.d[1] = u.y; raw.d[2] = u.z; raw.d[3] = u.w;
         raw.d[4] = v.x; raw.d[5] = v.y; raw.d[6] = v.z; raw.d[7] = v.w;
       }
       if (crow) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_C + lane * 32);
-        const uint4 v = *reinterpret_cast<const uint4*>(sp + WS_C + lane * 32 + 16);
+        const unsigned char* cp = sp + SG_C + warp * (GROUP * 4) + lane * 32;
+        const uint4 u = *reinterpret_cast<const uint4*>(cp);
+        const uint4 v = *reinterpret_cast<const uint4*>(cp + 16);
         raw.c[0] = u.x; raw.c[1] = u.y; raw.c[2] = u.z; raw.c[3] = u.w;
         raw.c[4] = v.x; raw.c[5] = v.y; raw.c[6] = v.z; raw.c[7] = v.w;
       }
       if (brow) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sp + WS_B + lane * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(sp + SG_B + warp * (GROUP * 2) + lane * 16);
         raw.b[0] = u.x; raw.b[1] = u.y; raw.b[2] = u.z; raw.b[3] = u.w;
       }
-      if (grow) raw.g = sp[WS_G + lane];
+      if (grow) raw.g = sp[SG_G + warp * (GROUP / 8) + lane];
     } else {
       load_group<DM, INDIRECT>(a, rc, slot, xrow, c, nv, raw);
     }
     process_group(raw, c, nv, k);
     if (staged) {
-      // every lane has consumed its loads of this stage: refill it
+      // this warp has consumed its slice of the stage; the last of the NW warps refills it
       __syncwarp();
-      if (k + WST < kfull) issue(k + WST);
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&st.rel[k % STAGES], 1) == NW - 1) {
+          atomicExch(&st.rel[k % STAGES], 0);
+          if (k + STAGES < nchunks) {
+            __threadfence_block();
+            fence_proxy_async();
+            issue_chunk(k + STAGES);
+          }
+        }
+      }
     }
   }
   if (werr) atomicOr(ws.error, 1u);
@@ -1182,7 +1240,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       __threadfence();
     }
   } else {
-    if (w.qn) wtk_absorb(w, q, lane);
+    if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
     if (warp == 0) {
@@ -1196,6 +1254,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
       __syncthreads();
       wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
+      tq = false;  // the exact path pushes final keys
       for (int gg = warp; gg < ngroups; gg += NW) {
         Raw8 raw;
         load_group<DM, INDIRECT>(a, rc, slot, xrow, gcol(gg), gvalid(gg), raw);
@@ -1231,7 +1290,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     for (int s = lane; s < splits; s += 32) b = umax(b, ldcg64(lists + (int64_t)s * kMaxK));
     b = warp_max_u64(b);
     int64_t token = greedy_col(b, log2bn);
-    if (a.d2t) token = load_index(a.d2t, a.d2t_dtype, token);
+    // a column outside the row can only come from a workspace that was not zero-filled
+    if (token < 0 || token >= a.vocab_size) token = -1;
+    else if (a.d2t) token = load_index(a.d2t, a.d2t_dtype, token);
     if (lane == 0) {
       if ((flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
         int32_t* d = P.decode_counts + slot * P.counts_stride + token;
@@ -1248,6 +1309,17 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   float v[4];
   int64_t idx[4];
   decode_keys(k, v, idx);
+  // a column outside the row can only come from a workspace that was not zero-filled: such a
+  // candidate is dropped instead of being gathered
+  bool bad[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bad[j] = idx[j] < 0 || idx[j] >= a.vocab_size;
+    if (bad[j]) {
+      v[j] = __int_as_float(0xff800000);
+      idx[j] = 0;
+    }
+  }
   int64_t tok[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) tok[j] = a.d2t ? load_index(a.d2t, a.d2t_dtype, idx[j]) : idx[j];
@@ -1256,11 +1328,12 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   bool off[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    off[j] = a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab);
+    off[j] = bad[j] || (a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab));
     if (!(flags & SONIC_FLAG_PHILOX) && !off[j]) noise[j] = a.gumbel[slot * a.gumbel_stride + tok[j]];
   }
   const float vmax = __shfl_sync(kFull, v[0], 0);
-  if (ind & 0x380) warp_masking(st.mp, ind, v, vmax, lane);
+  float ev[4];
+  const bool have_e = (ind & 0x380) ? warp_masking(st.mp, ind, v, vmax, lane, ev) : false;
   float diff[4];
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
@@ -1278,7 +1351,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
   if (flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
     float ls[4];
-    warp_log_softmax(v, __shfl_sync(kFull, v[0], 0), ls);
+    warp_log_softmax(v, vmax, ls, have_e && vmax != __int_as_float(0xff800000), ev);
     if ((flags & SONIC_FLAG_LOGPROBS) && a.logprobs) {
       const float lsel = warp_pick128(ls, sel);
       if (lane == 0) store_float(a.logprobs, a.logprobs_dtype, r * a.logprobs_stride, lsel);
@@ -1298,7 +1371,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const float p = dexp(ls[j]);
-        if (a.target_vocab <= 0 || (tok[j] >= 0 && tok[j] < a.target_vocab))
+        if (!bad[j] && (a.target_vocab <= 0 || (tok[j] >= 0 && tok[j] < a.target_vocab)))
           store_float(a.probabilities, a.probabilities_dtype, slot * a.probabilities_stride + tok[j], p);
       }
     }
@@ -1870,7 +1943,8 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
       int64_t idx[4];
       decode_keys(k, v, idx);
       const float vmax = __shfl_sync(kFull, v[0], 0);
-      if (ind & 0x380) warp_masking(load_mask_params(P, slot), ind, v, vmax, lane);
+      float ev[4];
+      if (ind & 0x380) warp_masking(load_mask_params(P, slot), ind, v, vmax, lane, ev);
       float ls[4];
       warp_log_softmax(v, vmax, ls);
 #pragma unroll
@@ -1939,8 +2013,12 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
       const int i = 4 * lane + j;
       const float sc = sm.prob[accepted][i];
       pos[j] = sm.cand[accepted][i];
+      // a column outside the row can only come from a workspace that was not zero-filled
+      const bool bad = pos[j] < 0 || pos[j] >= a.vocab_size;
       float rr;
-      if (accepted == T - 1)
+      if (bad)
+        rr = 0.0f;
+      else if (accepted == T - 1)
         rr = sc;
       else if (!stochastic_draft)
         rr = (pos[j] == sm.drafted[accepted]) ? 0.0f : sc;
@@ -1951,7 +2029,7 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
         rr = __fsub_rn(sc, q);
         rr = rr < 0.0f ? 0.0f : (rr > 1.0f ? 1.0f : rr);
       }
-      const float g = bf2f(a.gumbel[slot * a.gumbel_stride + accepted * a.gumbel_step_stride + pos[j]]);
+      const float g = bad ? 0.0f : bf2f(a.gumbel[slot * a.gumbel_stride + accepted * a.gumbel_step_stride + pos[j]]);
       score[j] = __fsub_rn(dlog(rr), g);
     }
     const int sel = warp_argmax128(score, lane);
@@ -2133,7 +2211,7 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
-  const size_t ring = mode == kTma ? (size_t)NW * WST * WS_BYTES : 0;
+  const size_t ring = mode == kTma ? (size_t)STAGES * SG_STAGE : 0;
   cudaError_t e;
   if (ind)
     e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws)

@@ -332,8 +332,14 @@ def topk_workspace_bytes(rows: int, vocab_size: int) -> int:
 
 
 def new_workspace(nbytes: int, device: torch.device) -> Tensor:
-    """Zero-filled workspace (the kernels keep their tickets at zero between calls)."""
-    return torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    """Zero-filled workspace (the kernels keep their tickets at zero between calls).
+
+    The zero fill runs on the current stream. Outside graph capture the call waits for it,
+    so that a later call on any other stream finds the tickets at zero."""
+    ws = torch.zeros(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+    if ws.is_cuda and not torch.cuda.is_current_stream_capturing():
+        torch.cuda.current_stream(ws.device).synchronize()
+    return ws
 
 
 def _stream(device: torch.device) -> int:
