@@ -115,7 +115,9 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def dist_setup():
+def dist_setup(backend: str = "nccl"):
+    """torchrun environment -> (world, rank, local rank); one process per GPU over NCCL (the
+    tests use gloo on CPU)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -124,9 +126,12 @@ def dist_setup():
 
         import torch.distributed as dist
 
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=60))
     return world, rank, local
 
 
@@ -145,7 +150,14 @@ def barrier(world: int):
         import torch.distributed as dist
 
         dist.barrier()
-    torch.cuda.synchronize()
+    if torch.cuda.is_available():
+        torch.cuda.synchronize()
+
+
+def weak_rows_per_s(world: int, rows_per_rank: int, steps: int, max_total_ms: float) -> float:
+    """Whole-job rows/s: every rank samples its own rows each step; the job time is the
+    slowest rank's."""
+    return world * rows_per_rank * steps / (max_total_ms / 1e3)
 
 
 # ------------------------------------------------------------------------------------------
@@ -197,7 +209,7 @@ def run_ours(args) -> None:
     per_step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = max_over_ranks(sum(per_step_ms), world, dev)
     ms_per_step = total_ms / args.steps
-    rows_per_s = world * BATCH * args.steps / (total_ms / 1e3)
+    rows_per_s = weak_rows_per_s(world, BATCH, args.steps, total_ms)
 
     # end to end: host logits in pinned memory -> device -> sampler -> tokens/logprobs to host
     host_logits = logits.cpu().pin_memory()
@@ -230,7 +242,7 @@ def run_ours(args) -> None:
         ee[i].record(stream)
     barrier(world)
     e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(es, ee)), world, dev)
-    e2e_rows = world * BATCH * e2e_steps / (e2e_ms / 1e3)
+    e2e_rows = weak_rows_per_s(world, BATCH, e2e_steps, e2e_ms)
     del graph, e2e_graph
 
     if rank != 0:
@@ -329,9 +341,14 @@ def cpu_baseline(logits_h, buffers, budget_s: float = 15.0, threads: int | None 
                       f"{len(chunks)} threads over row slices"}
 
 
+REFERENCE_BUDGET_S = 90.0  # bound on the timed part of the reference arm
+
+
 def run_reference(args) -> None:
-    """Each step: one full config-2 batch (64 rows) through the CPU restatement, rows spread
-    over all host threads."""
+    """Each step: a bounded sample of the config-2 batch (whole rows, at most all 64)
+    through the CPU restatement, rows spread over all host threads. The sample is sized so
+    that the `--steps` timed steps take about REFERENCE_BUDGET_S seconds. Under torchrun only
+    rank 0 runs; the other ranks exit at once."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -343,16 +360,26 @@ def run_reference(args) -> None:
     w = workloads.config2("cpu", seed=1000)
     logits_h, hb = w["logits"], w["buffers"]
     threads = os.cpu_count() or 1
-    chunks = [c for c in (range(i * BATCH // threads, (i + 1) * BATCH // threads) for i in range(threads)) if len(c)]
-    with ThreadPoolExecutor(max_workers=len(chunks)) as pool:
-        run = lambda: list(pool.map(lambda c: _oracle_rows(logits_h, hb, c), chunks))  # noqa: E731
-        for _ in range(args.warmup):
-            run()
+
+    def chunks_of(rows: int):
+        return [c for c in (range(i * rows // threads, (i + 1) * rows // threads) for i in range(threads)) if len(c)]
+
+    with ThreadPoolExecutor(max_workers=threads) as pool:
+        def run(rows: int):
+            list(pool.map(lambda c: _oracle_rows(logits_h, hb, c), chunks_of(rows)))
+
+        t0 = time.perf_counter()
+        run(BATCH)  # one full batch (also the first warm-up step) sizes the sample
+        per_row = (time.perf_counter() - t0) / BATCH
+        rows = max(1, min(BATCH, int(REFERENCE_BUDGET_S / max(args.steps, 1) / per_row)))
+        for _ in range(args.warmup - 1):
+            run(rows)
         t0 = time.perf_counter()
         for _ in range(args.steps):
-            run()
+            run(rows)
         dt = time.perf_counter() - t0
-    value = round(BATCH * args.steps / dt, 1)
+    chunks = chunks_of(rows)
+    value = round(rows * args.steps / dt, 1)
     line = {
         "metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
@@ -360,7 +387,7 @@ def run_reference(args) -> None:
         "config": {"workload": WORKLOAD, "rows_per_gpu": BATCH, "vocab": VOCAB},
         "impl": "reference",
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": len(chunks), "kind": "port",
-                         "sample": f"{args.steps} full batches of config 2 (B=64, V=128256), "
+                         "sample": f"{args.steps} steps of {rows} of the 64 config-2 rows (V=128256) each, "
                                    f"{len(chunks)} threads over row slices"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }

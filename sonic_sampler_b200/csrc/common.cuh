@@ -392,7 +392,7 @@ __device__ __forceinline__ float bf2_lo(uint32_t x) { return __uint_as_float(x <
 __device__ __forceinline__ float bf2_hi(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
 
 // ---------------------------------------------------------------------------------------
-// bulk (TMA) global -> shared copies completed on an mbarrier. No cluster multicast.
+// bulk (TMA) global -> shared copies completed on an mbarrier; every CTA loads its own data.
 // ---------------------------------------------------------------------------------------
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
