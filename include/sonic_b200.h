@@ -221,6 +221,24 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* args, void* stream);
 sonic_status sonic_fused_multistep(const SonicMultistepArgs* args, void* stream);
 sonic_status sonic_bounded_topk(const SonicTopKArgs* args, void* stream);
 
+/* Vocab-sharded singular sampling in three steps, for a vocabulary split over `world` ranks
+ * (rank r holds the logits columns [r * shard, r * shard + local), args->shard_offset = r * shard).
+ * The reference's own sharded path is unfinished (interface/functional/singular.py:145-149
+ * writes every shard at column 0; ops/singular.py:61-66 decodes greedy indices wrongly); these
+ * entry points replace it.
+ *   1. sonic_shard_candidates: streams this rank's shard exactly as sonic_fused_singular does
+ *      and writes, per row, the shard's 128 best candidates as sorted 64-bit keys with GLOBAL
+ *      columns to keys[rows][128] (greedy rows too). No selection, no output but `keys`.
+ *   2. the caller all-gathers keys over the ranks into gathered[world][rows][128] (one
+ *      ncclAllGather / torch.distributed.all_gather_into_tensor).
+ *   3. sonic_merge_candidates: merges the world lists of every row and runs selection, logprobs
+ *      and count updates exactly as sonic_fused_singular; args->vocab_size is the full
+ *      vocabulary and the noise covers it, so every rank computes the same tokens. Greedy rows
+ *      take the largest value with the lowest global column. */
+sonic_status sonic_shard_candidates(const SonicSingularArgs* args, uint64_t* keys, void* stream);
+sonic_status sonic_merge_candidates(const SonicSingularArgs* args, const uint64_t* gathered, int32_t world,
+                                    void* stream);
+
 /* sonic_fused_singular for callers that cannot allocate device memory (an engine whose KV
  * cache already holds all free HBM, a cgo / JNI binding without the framework's allocator,
  * a loop that cannot afford cudaMalloc's possible device synchronisation). No counterpart

@@ -173,6 +173,8 @@ EXPORTED_SYMBOLS = (
     "sonic_fused_multistep",
     "sonic_bounded_topk",
     "sonic_fused_singular_static",
+    "sonic_shard_candidates",
+    "sonic_merge_candidates",
     "sonic_abi_version",
     "sonic_last_error",
 )
@@ -199,6 +201,10 @@ def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(argt), _vp]
         fn.restype = _i32
+    lib.sonic_shard_candidates.argtypes = [ctypes.POINTER(SingularArgs), _vp, _vp]
+    lib.sonic_shard_candidates.restype = _i32
+    lib.sonic_merge_candidates.argtypes = [ctypes.POINTER(SingularArgs), _vp, _i32, _vp]
+    lib.sonic_merge_candidates.restype = _i32
     lib.sonic_abi_version.argtypes = []
     lib.sonic_abi_version.restype = _i32
     lib.sonic_last_error.argtypes = []

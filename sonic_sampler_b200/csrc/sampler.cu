@@ -748,7 +748,7 @@ __device__ __forceinline__ int64_t key_column(uint64_t g) { return (int64_t)(0xf
 // Warp v folds lists v, v+8, ... (all its loads issued at once), then a 3-round tree over
 // shared memory (`xchg`, NW x 128 u64) combines the warp results. Block-wide.
 __device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* xchg, int warp, int lane,
-                                  uint64_t (&out)[4]) {
+                                  uint64_t (&out)[4], int64_t list_stride = kMaxK) {
   uint64_t acc[4] = {0, 0, 0, 0};
   if (warp < splits) {
     constexpr int PER = MAX_SPLITS / NW;
@@ -757,7 +757,7 @@ __device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* x
     for (int t = 0; t < PER; ++t) {
       const int s = warp + t * NW;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) pre[t][j] = s < splits ? ldcg64(lists + (int64_t)s * kMaxK + 4 * lane + j) : 0ull;
+      for (int j = 0; j < 4; ++j) pre[t][j] = s < splits ? ldcg64(lists + (int64_t)s * list_stride + 4 * lane + j) : 0ull;
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[j] = pre[0][j];
@@ -942,13 +942,95 @@ __device__ __forceinline__ void load_group(const SonicSingularArgs& a, const Row
 }
 
 // ---------------------------------------------------------------------------------------
+// selection epilogue of one row (ops/base.py:66-129, ops/singular.py:259-358) on its merged,
+// sorted top-128 keys held 4 per lane by one warp
+// ---------------------------------------------------------------------------------------
+
+__device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r, int64_t slot, uint32_t ind,
+                                           const MaskParams& mp, const uint64_t (&k)[4], int lane) {
+  const SonicSamplingParams& P = a.params;
+  const uint32_t flags = a.flags;
+  float v[4];
+  int64_t idx[4];
+  decode_keys(k, v, idx);
+  // a column outside the row can only come from a workspace that was not zero-filled: such a
+  // candidate is dropped instead of being gathered
+  bool bad[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    bad[j] = idx[j] < 0 || idx[j] >= a.vocab_size;
+    if (bad[j]) {
+      v[j] = __int_as_float(0xff800000);
+      idx[j] = 0;
+    }
+  }
+  int64_t tok[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) tok[j] = a.d2t ? load_index(a.d2t, a.d2t_dtype, idx[j]) : idx[j];
+  // noise loads first: their latency overlaps the masking
+  uint16_t noise[4] = {0, 0, 0, 0};
+  bool off[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    off[j] = bad[j] || (a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab));
+    if (!(flags & SONIC_FLAG_PHILOX) && !off[j]) noise[j] = a.gumbel[slot * a.gumbel_stride + tok[j]];
+  }
+  const float vmax = __shfl_sync(kFull, v[0], 0);
+  float ev[4];
+  const bool have_e = (ind & 0x380) ? warp_masking(mp, ind, v, vmax, lane, ev) : false;
+  float diff[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (flags & SONIC_FLAG_PHILOX)
+      diff[j] = __fsub_rn(v[j], philox_log_exponential(a.philox_seed, a.philox_offset, (uint32_t)slot,
+                                                        (uint32_t)tok[j]));
+    else
+      diff[j] = off[j] ? __int_as_float(0xff800000) : rbf(__fsub_rn(v[j], bf2f(noise[j])));
+  }
+  const int sel = warp_argmax128(diff, lane);
+  const int64_t token = warp_pick128(tok, sel);
+  if (lane == 0 && (flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
+    int32_t* d = P.decode_counts + slot * P.counts_stride + token;
+    *d = (flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+  }
+  if (flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
+    float ls[4];
+    warp_log_softmax(v, vmax, ls, have_e && vmax != __int_as_float(0xff800000), ev);
+    if ((flags & SONIC_FLAG_LOGPROBS) && a.logprobs) {
+      const float lsel = warp_pick128(ls, sel);
+      if (lane == 0) store_float(a.logprobs, a.logprobs_dtype, r * a.logprobs_stride, lsel);
+      if (a.max_top_logprobs > 0 && (ind & 0x400) && a.top_logprob_values && P.top_logprobs) {
+        const int z = min(mp.top_logprobs, a.max_top_logprobs);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int i = 4 * lane + j;
+          if (i < z) {
+            store_float(a.top_logprob_values, a.logprobs_dtype, r * a.top_stride + i, ls[j]);
+            a.top_logprob_tokens[r * a.top_stride + i] = (int32_t)tok[j];
+          }
+        }
+      }
+    }
+    if ((flags & SONIC_FLAG_PROBABILITIES) && a.probabilities) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float p = dexp(ls[j]);
+        if (!bad[j] && (a.target_vocab <= 0 || (tok[j] >= 0 && tok[j] < a.target_vocab)))
+          store_float(a.probabilities, a.probabilities_dtype, slot * a.probabilities_stride + tok[j], p);
+      }
+    }
+  }
+  if (lane == 0) a.tokens[r * a.tokens_stride] = (int32_t)token;
+}
+
+// ---------------------------------------------------------------------------------------
 // fused singular: prologue + top-128 per split + merge + selection
 // (ops/prologue.py:272 + ops/singular.py:154)
 // ---------------------------------------------------------------------------------------
 
 template <int MODE, bool INDIRECT>
 __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
-                                                      Workspace ws) {
+                                                      Workspace ws, uint64_t* cand_out) {
   __shared__ __align__(16) RowSmem<uint32_t> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -968,7 +1050,8 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
   const uint32_t ind = P.indicators[slot];
   const RowConsts rc = row_consts(P, slot, ind);
-  const bool greedy = (ind & 0x40) != 0;
+  // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
+  const bool greedy = (ind & 0x40) != 0 && !cand_out;
   const int ntok = (a.drafted_tokens && rc.nd.dec) ? a.lookahead : 0;
   if (tid < ntok) st.toks[tid] = a.drafted_tokens[slot * a.drafted_stride + tid];
   // streams of the bulk-copy ring (see below)
@@ -1272,7 +1355,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
         const uint64_t key = to_global<uint32_t>(fin[j], c0);
         stcg64(out + 4 * lane + j, key);
         // warm L2 with the noise the merge will gather for this candidate
-        if (key && !(a.flags & SONIC_FLAG_PHILOX) && !a.d2t &&
+        if (key && !cand_out && !(a.flags & SONIC_FLAG_PHILOX) && !a.d2t &&
             (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
           asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
       }
@@ -1306,77 +1389,56 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   uint64_t k[4];
   block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
   if (warp != 0) return;
-  float v[4];
-  int64_t idx[4];
-  decode_keys(k, v, idx);
-  // a column outside the row can only come from a workspace that was not zero-filled: such a
-  // candidate is dropped instead of being gathered
-  bool bad[4];
+  if (cand_out) {
+    // vocab-sharded step 1: the row's 128 best candidates of this shard, global columns
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    bad[j] = idx[j] < 0 || idx[j] >= a.vocab_size;
-    if (bad[j]) {
-      v[j] = __int_as_float(0xff800000);
-      idx[j] = 0;
+    for (int j = 0; j < 4; ++j) {
+      uint64_t key = k[j];
+      if (key) key = (key & 0xffffffff00000000ull) | (uint64_t)(0xffffffffu - (uint32_t)(key_column(key) + shard));
+      stcg64(cand_out + r * kMaxK + 4 * lane + j, key);
     }
+    return;
   }
-  int64_t tok[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) tok[j] = a.d2t ? load_index(a.d2t, a.d2t_dtype, idx[j]) : idx[j];
-  // noise loads first: their latency overlaps the masking
-  uint16_t noise[4] = {0, 0, 0, 0};
-  bool off[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    off[j] = bad[j] || (a.target_vocab > 0 && (tok[j] < 0 || tok[j] >= a.target_vocab));
-    if (!(flags & SONIC_FLAG_PHILOX) && !off[j]) noise[j] = a.gumbel[slot * a.gumbel_stride + tok[j]];
+  select_row(a, r, slot, ind, st.mp, k, lane);
+}
+
+// ---------------------------------------------------------------------------------------
+// vocab-sharded singular, step 3: merge the ranks' candidate lists of a row (gathered
+// [world][rows][128] keys with global columns) and select, identically on every rank
+// ---------------------------------------------------------------------------------------
+
+__global__ void __launch_bounds__(NT) merge_candidates_kernel(const SonicSingularArgs a, const uint64_t* gathered,
+                                                              int world) {
+  __shared__ __align__(16) uint64_t xchg[NW][kMaxK];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t r = blockIdx.x;
+  const SonicSamplingParams& P = a.params;
+  pdl_wait();
+  const int64_t slot = load_slot(P, r);
+  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
+    if (threadIdx.x == 0) a.tokens[r * a.tokens_stride] = -1;
+    return;
   }
-  const float vmax = __shfl_sync(kFull, v[0], 0);
-  float ev[4];
-  const bool have_e = (ind & 0x380) ? warp_masking(st.mp, ind, v, vmax, lane, ev) : false;
-  float diff[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (flags & SONIC_FLAG_PHILOX)
-      diff[j] = __fsub_rn(v[j], philox_log_exponential(a.philox_seed, a.philox_offset, (uint32_t)slot,
-                                                        (uint32_t)tok[j]));
-    else
-      diff[j] = off[j] ? __int_as_float(0xff800000) : rbf(__fsub_rn(v[j], bf2f(noise[j])));
-  }
-  const int sel = warp_argmax128(diff, lane);
-  const int64_t token = warp_pick128(tok, sel);
-  if (lane == 0 && (flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
-    int32_t* d = P.decode_counts + slot * P.counts_stride + token;
-    *d = (flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
-  }
-  if (flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
-    float ls[4];
-    warp_log_softmax(v, vmax, ls, have_e && vmax != __int_as_float(0xff800000), ev);
-    if ((flags & SONIC_FLAG_LOGPROBS) && a.logprobs) {
-      const float lsel = warp_pick128(ls, sel);
-      if (lane == 0) store_float(a.logprobs, a.logprobs_dtype, r * a.logprobs_stride, lsel);
-      if (a.max_top_logprobs > 0 && (ind & 0x400) && a.top_logprob_values && P.top_logprobs) {
-        const int z = min(st.mp.top_logprobs, a.max_top_logprobs);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int i = 4 * lane + j;
-          if (i < z) {
-            store_float(a.top_logprob_values, a.logprobs_dtype, r * a.top_stride + i, ls[j]);
-            a.top_logprob_tokens[r * a.top_stride + i] = (int32_t)tok[j];
-          }
-        }
+  const uint32_t ind = P.indicators[slot];
+  uint64_t k[4];
+  block_merge_lists(gathered + r * kMaxK, world, &xchg[0][0], warp, lane, k, (int64_t)a.rows * kMaxK);
+  pdl_trigger();
+  if (warp != 0) return;
+  if (ind & 0x40) {
+    // greedy: the best candidate (largest value, lowest global column)
+    const uint64_t best = __shfl_sync(kFull, k[0], 0);
+    int64_t token = best ? key_column(best) : -1;
+    if (token >= a.vocab_size) token = -1;
+    if (lane == 0) {
+      if ((a.flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
+        int32_t* d = P.decode_counts + slot * P.counts_stride + token;
+        *d = (a.flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
       }
+      a.tokens[r * a.tokens_stride] = (int32_t)token;
     }
-    if ((flags & SONIC_FLAG_PROBABILITIES) && a.probabilities) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float p = dexp(ls[j]);
-        if (!bad[j] && (a.target_vocab <= 0 || (tok[j] >= 0 && tok[j] < a.target_vocab)))
-          store_float(a.probabilities, a.probabilities_dtype, slot * a.probabilities_stride + tok[j], p);
-      }
-    }
+    return;
   }
-  if (lane == 0) a.tokens[r * a.tokens_stride] = (int32_t)token;
+  select_row(a, r, slot, ind, load_mask_params(P, slot), k, lane);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -2173,20 +2235,22 @@ size_t sonic_bounded_topk_workspace_size(const SonicTopKArgs* a) {
   return workspace_bytes(a->rows, a->rows, singular_plan(a->rows, a->vocab_size).splits);
 }
 
-sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
-  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
-  if (a->rows == 0) return SONIC_OK;
+}  // extern "C"
+
+namespace sonic {
+
+// Host checks shared by the singular entry points (selection arguments only when `selects`).
+static sonic_status check_singular(const SonicSingularArgs* a, bool selects) {
   if (a->rows < 0 || a->rows > 65535) return fail(SONIC_ERR_INVALID_ARGUMENT, "rows must be in [0, 65535]");
   if (a->vocab_size < kMaxK) return fail(SONIC_ERR_INVALID_ARGUMENT, "vocab_size must be >= 128");
   if (sonic_status s = check_block_n(a->block_n)) return s;
   if (sonic_status s = check_params(a->params)) return s;
-  if (!a->logits || a->logits_dtype != SONIC_DTYPE_BF16)
-    return fail(SONIC_ERR_INVALID_ARGUMENT, "logits must be a non-NULL bf16 tensor");
   if (!a->tokens) return fail(SONIC_ERR_INVALID_ARGUMENT, "tokens must not be NULL");
   if (a->lookahead < 0 || a->lookahead > SONIC_MAX_LOOKAHEAD)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "lookahead must be in [0, 15]");
   if (a->d2t && a->d2t_dtype != SONIC_DTYPE_I32 && a->d2t_dtype != SONIC_DTYPE_I64)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "d2t dtype must be i32 or i64");
+  if (!selects) return SONIC_OK;
   if (!(a->flags & SONIC_FLAG_PHILOX) && !a->gumbel)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel noise must not be NULL without SONIC_FLAG_PHILOX");
   if ((a->flags & SONIC_FLAG_UPDATE_COUNTS) && !a->params.decode_counts)
@@ -2198,6 +2262,14 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "max_top_logprobs must be in [0, 128]");
   if (a->logprobs_dtype != SONIC_DTYPE_BF16 && a->logprobs_dtype != SONIC_DTYPE_F32)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logprobs dtype must be bf16 or f32");
+  return SONIC_OK;
+}
+
+// The singular launch; with `cand` the last CTA of a row writes the row's top-128 keys
+// (global columns) there instead of selecting.
+static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, uint64_t* cand, const char* what) {
+  if (!a->logits || a->logits_dtype != SONIC_DTYPE_BF16)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "logits must be a non-NULL bf16 tensor");
   const Plan p = singular_plan(a->rows, a->vocab_size);
   const size_t need = workspace_bytes(a->rows, a->rows, p.splits);
   if (!a->workspace || a->workspace_bytes < need)
@@ -2214,15 +2286,48 @@ sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
   const size_t ring = mode == kTma ? (size_t)STAGES * SG_STAGE : 0;
   cudaError_t e;
   if (ind)
-    e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws)
-                     : launch(singular_kernel<kScalar, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws);
+    e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand)
+                     : launch(singular_kernel<kScalar, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
   else if (mode == kTma)
-    e = launch(singular_kernel<kTma, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws);
+    e = launch(singular_kernel<kTma, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
   else
-    e = mode == kVec ? launch(singular_kernel<kVec, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws)
-                     : launch(singular_kernel<kScalar, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws);
-  return check_launch(e, "sonic_fused_singular");
+    e = mode == kVec ? launch(singular_kernel<kVec, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand)
+                     : launch(singular_kernel<kScalar, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
+  return check_launch(e, what);
 }
+
+}  // namespace sonic
+
+extern "C" {
+
+sonic_status sonic_fused_singular(const SonicSingularArgs* a, void* stream) {
+  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
+  if (a->rows == 0) return SONIC_OK;
+  if (sonic_status s = check_singular(a, true)) return s;
+  return singular_launch(a, stream, nullptr, "sonic_fused_singular");
+}
+
+sonic_status sonic_shard_candidates(const SonicSingularArgs* a, uint64_t* keys, void* stream) {
+  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
+  if (a->rows == 0) return SONIC_OK;
+  if (!keys) return fail(SONIC_ERR_INVALID_ARGUMENT, "keys must not be NULL");
+  if (sonic_status s = check_singular(a, false)) return s;
+  return singular_launch(a, stream, keys, "sonic_shard_candidates");
+}
+
+sonic_status sonic_merge_candidates(const SonicSingularArgs* a, const uint64_t* gathered, int32_t world,
+                                    void* stream) {
+  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
+  if (a->rows == 0) return SONIC_OK;
+  if (!gathered) return fail(SONIC_ERR_INVALID_ARGUMENT, "gathered keys must not be NULL");
+  if (world < 1 || world > MAX_SPLITS) return fail(SONIC_ERR_INVALID_ARGUMENT, "world must be in [1, 32]");
+  if (sonic_status s = check_singular(a, true)) return s;
+  const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
+  const cudaError_t e = launch(merge_candidates_kernel, dim3(a->rows), 0, (cudaStream_t)stream, pdl, *a, gathered,
+                               (int)world);
+  return check_launch(e, "sonic_merge_candidates");
+}
+
 
 sonic_status sonic_bounded_topk(const SonicTopKArgs* a, void* stream) {
   if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");

@@ -104,9 +104,9 @@ def prepare_singular(
     """Resolve defaults, outputs and C-ABI arguments of `fused_singular` without launching.
     Works for host tensors too (no workspace is attached then)."""
     validate_count_update(update_counts, decode_counts)
-    if world_size > 1:
-        raise ValueError("vocab-sharded singular sampling is not available in this library yet; "
-                         "shard requests by rows")
+    if world_size > 1 and gumbel_noise is None and philox_seed is None:
+        raise ValueError("vocab-sharded sampling needs the full-vocabulary `gumbel_noise` (the same on every "
+                         "rank) or `philox_seed`")
 
     batch_size, vocab_size = logits.shape
     vocab_size = min(vocab_size, local_vocab or vocab_size)
@@ -159,9 +159,28 @@ def prepare_singular(
     return selection, args
 
 
-def fused_singular(logits: Tensor, indicators: Tensor, **kwargs) -> Selection:
-    """Same keywords as the reference's `fused_singular` (see `prepare_singular`)."""
+def fused_singular(logits: Tensor, indicators: Tensor, process_group=None, **kwargs) -> Selection:
+    """Same keywords as the reference's `fused_singular` (see `prepare_singular`).
+
+    With `world_size > 1` the vocabulary is sharded: this rank's `logits` hold the columns
+    [local_rank * shard_size, local_rank * shard_size + logits.size(1)), while buffers, noise
+    and outputs cover the whole vocabulary and are the same on every rank. Each rank extracts
+    its 128 best candidates per row, one all-gather over `process_group` (default: the world
+    group) exchanges them, and every rank merges and selects identically."""
     ops._require_cuda(logits)
     selection, args = prepare_singular(logits, indicators, **kwargs)
-    ops.launch_singular(args, logits.device)
+    world = int(kwargs.get("world_size", 1))
+    if world <= 1:
+        ops.launch_singular(args, logits.device)
+        return selection
+    import torch.distributed as dist
+
+    rows = logits.size(0)
+    keys = torch.empty(rows, 128, dtype=torch.int64, device=logits.device)
+    ops.launch_shard_candidates(args, keys, logits.device)
+    gathered = torch.empty(world, rows, 128, dtype=torch.int64, device=logits.device)
+    dist.all_gather_into_tensor(gathered, keys, group=process_group)
+    shard = int(kwargs.get("shard_size") or logits.size(1))
+    args.vocab_size = shard * world  # candidates carry global columns below this bound
+    ops.launch_merge_candidates(args, gathered, world, logits.device)
     return selection

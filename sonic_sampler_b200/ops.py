@@ -357,6 +357,26 @@ def launch_singular(args: SingularArgs, device: torch.device) -> None:
         _abi.check(lib.sonic_fused_singular(ctypes.byref(args), ctypes.c_void_p(_stream(device))), lib)
 
 
+def launch_shard_candidates(args: SingularArgs, keys: Tensor, device: torch.device) -> None:
+    """Vocab-sharded step 1: this rank's top-128 candidate keys per row into `keys` [rows, 128] int64."""
+    _require(keys.dtype == torch.int64 and keys.is_contiguous() and keys.numel() >= args.rows * 128,
+             "keys must be a contiguous int64 tensor of rows x 128")
+    lib = _abi.load_library()
+    with torch.cuda.device(device):
+        _abi.check(lib.sonic_shard_candidates(ctypes.byref(args), ctypes.c_void_p(keys.data_ptr()),
+                                              ctypes.c_void_p(_stream(device))), lib)
+
+
+def launch_merge_candidates(args: SingularArgs, gathered: Tensor, world: int, device: torch.device) -> None:
+    """Vocab-sharded step 3: merge `gathered` [world, rows, 128] int64 keys and select."""
+    _require(gathered.dtype == torch.int64 and gathered.is_contiguous() and gathered.numel() >= world * args.rows * 128,
+             "gathered must be a contiguous int64 tensor of world x rows x 128")
+    lib = _abi.load_library()
+    with torch.cuda.device(device):
+        _abi.check(lib.sonic_merge_candidates(ctypes.byref(args), ctypes.c_void_p(gathered.data_ptr()), int(world),
+                                              ctypes.c_void_p(_stream(device))), lib)
+
+
 def launch_multistep(args: MultistepArgs, device: torch.device) -> None:
     lib = _abi.load_library()
     with torch.cuda.device(device):
