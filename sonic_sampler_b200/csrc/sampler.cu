@@ -796,14 +796,11 @@ __device__ void block_merge_lists(const uint64_t* lists, int splits, uint64_t* x
 
 constexpr int GROUP = VPT * 32;  // columns of one warp group
 constexpr int PF_GROUPS = 4;     // L2 prefetch distance of direct loads, in groups of one warp
-// bulk-copy stage layout (bytes) of one 2048-column chunk: logits, decode counts, context
-// counts, bias, grammar words
-constexpr int SG_X = 0;
-constexpr int SG_D = SG_X + CH * 2;
-constexpr int SG_C = SG_D + CH * 4;
-constexpr int SG_B = SG_C + CH * 4;
-constexpr int SG_G = SG_B + CH * 2;
-constexpr int SG_STAGE = SG_G + CH / 8;  // 24832
+// bytes of one 2048-column chunk with every stream: logits, decode counts, context counts, bias
+// (2 + 4 + 4 + 2 bytes a column) and grammar words
+constexpr int SG_STAGE = CH * 12 + CH / 8;     // 24832
+constexpr int RING_BYTES = STAGES * SG_STAGE;  // the ring's shared memory
+constexpr int MAX_RING_STAGES = 16;            // stages of rows with fewer streams (logits only: 16)
 
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
@@ -862,8 +859,8 @@ struct RowSmem {
   int flag;
   unsigned long long best;
   int32_t toks[SONIC_MAX_LOOKAHEAD + 1];
-  uint64_t bars[STAGES];  // bulk-copy stage filled
-  int rel[STAGES];        // warps done with the stage
+  uint64_t bars[MAX_RING_STAGES];  // bulk-copy stage filled
+  int rel[MAX_RING_STAGES];        // warps done with the stage
 };
 
 // After an absorb: the warp's new threshold candidates are its own 128th key value and the
@@ -1061,30 +1058,36 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
   const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
   const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
-  const uint32_t tx = CH * 2 + (drow ? CH * 4 : 0) + (crow ? CH * 4 : 0) + (brow ? CH * 2 : 0) + (grow ? CH / 8 : 0);
-  auto issue_chunk = [&](int i) {  // one thread
-    unsigned char* sp = smem_ring + (i % STAGES) * SG_STAGE;
-    uint64_t* bar = &st.bars[i % STAGES];
+  // stage layout of this row: only the streams it reads, as many stages as fit the ring
+  const int sg_d = CH * 2;
+  const int sg_c = sg_d + (drow ? CH * 4 : 0);
+  const int sg_b = sg_c + (crow ? CH * 4 : 0);
+  const int sg_g = sg_b + (brow ? CH * 2 : 0);
+  const int sg_stage = sg_g + (grow ? CH / 8 : 0);  // = the bytes of one chunk (multiple of 256)
+  const int nst = min(MAX_RING_STAGES, RING_BYTES / sg_stage);
+  auto issue_chunk = [&](int i, int stage) {  // one thread
+    unsigned char* sp = smem_ring + stage * sg_stage;
+    uint64_t* bar = &st.bars[stage];
     const int64_t cc = c0 + (int64_t)i * CH;
-    mbar_expect_tx(bar, tx);
-    bulk_load(sp + SG_X, xrow + cc, CH * 2, bar);
-    if (drow) bulk_load(sp + SG_D, drow + cc + shard, CH * 4, bar);
-    if (crow) bulk_load(sp + SG_C, crow + cc + shard, CH * 4, bar);
-    if (brow) bulk_load(sp + SG_B, brow + cc + shard, CH * 2, bar);
-    if (grow) bulk_load(sp + SG_G, grow + (cc + shard) / 32, CH / 8, bar);
+    mbar_expect_tx(bar, (uint32_t)sg_stage);
+    bulk_load(sp, xrow + cc, CH * 2, bar);
+    if (drow) bulk_load(sp + sg_d, drow + cc + shard, CH * 4, bar);
+    if (crow) bulk_load(sp + sg_c, crow + cc + shard, CH * 4, bar);
+    if (brow) bulk_load(sp + sg_b, brow + cc + shard, CH * 2, bar);
+    if (grow) bulk_load(sp + sg_g, grow + (cc + shard) / 32, CH / 8, bar);
   };
   if (tid == 0) {
     st.best = 0ull;
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
     if (MODE == kTma) {
-      for (int i = 0; i < STAGES; ++i) {
+      for (int i = 0; i < nst; ++i) {
         mbar_init(&st.bars[i], 1);
         st.rel[i] = 0;
       }
       mbar_fence_init();
       const int nch = (int)((c1 - c0) / CH);
-      for (int i = 0; i < min(nch, STAGES); ++i) issue_chunk(i);
+      for (int i = 0; i < min(nch, nst); ++i) issue_chunk(i, i);
     }
   }
   __syncthreads();
@@ -1227,19 +1230,19 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
     // columns whose counts are zero (their value needs no penalty), bound 128 distinct keys.
     if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
-    const uint4 xq = *reinterpret_cast<const uint4*>(smem_ring + SG_X + warp * (GROUP * 2) + lane * 16);
+    const uint4 xq = *reinterpret_cast<const uint4*>(smem_ring + warp * (GROUP * 2) + lane * 16);
     uint32_t y[4] = {xq.x, xq.y, xq.z, xq.w};
     if (brow) {
-      const uint4 bq = *reinterpret_cast<const uint4*>(smem_ring + SG_B + warp * (GROUP * 2) + lane * 16);
+      const uint4 bq = *reinterpret_cast<const uint4*>(smem_ring + sg_b + warp * (GROUP * 2) + lane * 16);
       y[0] = bf2_add(y[0], bq.x);
       y[1] = bf2_add(y[1], bq.y);
       y[2] = bf2_add(y[2], bq.z);
       y[3] = bf2_add(y[3], bq.w);
     }
-    uint32_t ok = grow ? smem_ring[SG_G + warp * (GROUP / 8) + lane] : 0xffu;
+    uint32_t ok = grow ? smem_ring[sg_g + warp * (GROUP / 8) + lane] : 0xffu;
     if (drow) {
-      const int32_t* dp = reinterpret_cast<const int32_t*>(smem_ring + SG_D + warp * (GROUP * 4)) + 8 * lane;
-      const int32_t* cp = reinterpret_cast<const int32_t*>(smem_ring + SG_C + warp * (GROUP * 4)) + 8 * lane;
+      const int32_t* dp = reinterpret_cast<const int32_t*>(smem_ring + sg_d + warp * (GROUP * 4)) + 8 * lane;
+      const int32_t* cp = reinterpret_cast<const int32_t*>(smem_ring + sg_c + warp * (GROUP * 4)) + 8 * lane;
 #pragma unroll
       for (int j = 0; j < VPT; ++j)
         if ((dp[j] | (crow ? cp[j] : 0)) != 0) ok &= ~(1u << j);
@@ -1256,15 +1259,17 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     const float t = lane_max_min(st.vlm, lane);
     if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
   }
+  int stage = 0;
+  uint32_t phase = 0;
   for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     Raw8 raw;
     const bool staged = k < nchunks;
     if (staged) {
-      if (!mbar_wait_bounded(&st.bars[k % STAGES], (uint32_t)(k / STAGES) & 1u, WAIT_LIMIT)) werr = true;
-      const unsigned char* sp = smem_ring + (k % STAGES) * SG_STAGE;
-      const uint4 xq = *reinterpret_cast<const uint4*>(sp + SG_X + warp * (GROUP * 2) + lane * 16);
+      if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+      const unsigned char* sp = smem_ring + stage * sg_stage;
+      const uint4 xq = *reinterpret_cast<const uint4*>(sp + warp * (GROUP * 2) + lane * 16);
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) raw.d[j] = raw.c[j] = 0;
@@ -1272,24 +1277,24 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       for (int p = 0; p < 4; ++p) raw.b[p] = 0;
       raw.g = 0xffu;
       if (drow) {
-        const unsigned char* dp = sp + SG_D + warp * (GROUP * 4) + lane * 32;
+        const unsigned char* dp = sp + sg_d + warp * (GROUP * 4) + lane * 32;
         const uint4 u = *reinterpret_cast<const uint4*>(dp);
         const uint4 v = *reinterpret_cast<const uint4*>(dp + 16);
         raw.d[0] = u.x; raw.d[1] = u.y; raw.d[2] = u.z; raw.d[3] = u.w;
         raw.d[4] = v.x; raw.d[5] = v.y; raw.d[6] = v.z; raw.d[7] = v.w;
       }
       if (crow) {
-        const unsigned char* cp = sp + SG_C + warp * (GROUP * 4) + lane * 32;
+        const unsigned char* cp = sp + sg_c + warp * (GROUP * 4) + lane * 32;
         const uint4 u = *reinterpret_cast<const uint4*>(cp);
         const uint4 v = *reinterpret_cast<const uint4*>(cp + 16);
         raw.c[0] = u.x; raw.c[1] = u.y; raw.c[2] = u.z; raw.c[3] = u.w;
         raw.c[4] = v.x; raw.c[5] = v.y; raw.c[6] = v.z; raw.c[7] = v.w;
       }
       if (brow) {
-        const uint4 u = *reinterpret_cast<const uint4*>(sp + SG_B + warp * (GROUP * 2) + lane * 16);
+        const uint4 u = *reinterpret_cast<const uint4*>(sp + sg_b + warp * (GROUP * 2) + lane * 16);
         raw.b[0] = u.x; raw.b[1] = u.y; raw.b[2] = u.z; raw.b[3] = u.w;
       }
-      if (grow) raw.g = sp[SG_G + warp * (GROUP / 8) + lane];
+      if (grow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
     } else {
       load_group<DM, INDIRECT>(a, rc, slot, xrow, c, nv, raw);
     }
@@ -1299,14 +1304,18 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
-        if (atomicAdd(&st.rel[k % STAGES], 1) == NW - 1) {
-          atomicExch(&st.rel[k % STAGES], 0);
-          if (k + STAGES < nchunks) {
+        if (atomicAdd(&st.rel[stage], 1) == NW - 1) {
+          atomicExch(&st.rel[stage], 0);
+          if (k + nst < nchunks) {
             __threadfence_block();
             fence_proxy_async();
-            issue_chunk(k + STAGES);
+            issue_chunk(k + nst, stage);
           }
         }
+      }
+      if (++stage == nst) {
+        stage = 0;
+        phase ^= 1u;
       }
     }
   }
@@ -2283,7 +2292,7 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
-  const size_t ring = mode == kTma ? (size_t)STAGES * SG_STAGE : 0;
+  const size_t ring = mode == kTma ? (size_t)RING_BYTES : 0;
   cudaError_t e;
   if (ind)
     e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand)
