@@ -284,81 +284,6 @@ __device__ __forceinline__ void warp_merge128_desc(K (&a)[4], const K (&b)[4], i
 }
 
 // ---------------------------------------------------------------------------------------
-// block radix select: threshold T such that exactly `want` of the n unique keys in `buf`
-// are >= T (n >= want). 8-bit digits from the top; stops early once the chosen digit's
-// bin holds exactly the keys still needed. `hist` is 256 ints of shared memory; `bcast`
-// 4 ints of shared memory. All threads of the block must call it.
-// ---------------------------------------------------------------------------------------
-
-template <typename K, int NT>
-__device__ K block_select(const K* buf, int n, int want, int* hist, int* bcast) {
-  constexpr int kBits = sizeof(K) * 8;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  K prefix = 0, pmask = 0;
-  int krem = want;
-#pragma unroll 1
-  for (int shift = kBits - 8; shift >= 0; shift -= 8) {
-    for (int i = tid; i < 256; i += NT) hist[i] = 0;
-    __syncthreads();
-    for (int base = 0; base < n; base += NT) {
-      const int i = base + tid;
-      K k = i < n ? buf[i] : (K)0;
-      bool ok = i < n && (k & pmask) == prefix;
-      int digit = (int)((k >> shift) & 0xff);
-      unsigned active = __ballot_sync(kFull, ok);
-      if (ok) {
-        unsigned peers = __match_any_sync(active, digit);
-        int leader = __ffs(peers) - 1;
-        if (lane == leader) atomicAdd(&hist[digit], __popc(peers));
-      }
-    }
-    __syncthreads();
-    if (warp == 0) {
-      // lane l owns bins 255-8l .. 248-8l (descending)
-      int c[8];
-      int tot = 0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        c[j] = hist[255 - 8 * lane - j];
-        tot += c[j];
-      }
-      int incl = tot;
-#pragma unroll
-      for (int d = 1; d < 32; d <<= 1) {
-        int y = __shfl_up_sync(kFull, incl, d);
-        if (lane >= d) incl += y;
-      }
-      int excl = incl - tot;
-      unsigned hit = __ballot_sync(kFull, incl >= krem);
-      int owner = __ffs(hit) - 1;
-      if (lane == owner) {
-        int above = excl;
-        int j = 0;
-        while (above + c[j] < krem) {
-          above += c[j];
-          ++j;
-        }
-        bcast[0] = 255 - 8 * lane - j;
-        bcast[1] = above;
-        bcast[2] = c[j];
-      }
-    }
-    __syncthreads();
-    const int d = bcast[0], above = bcast[1], cbin = bcast[2];
-    __syncthreads();
-    prefix |= (K)d << shift;
-    pmask |= (K)0xff << shift;
-    krem -= above;
-    if (cbin == krem) break;
-  }
-  return prefix;
-}
-
-}  // namespace sonic
-
-namespace sonic {
-
-// ---------------------------------------------------------------------------------------
 // packed bf16x2 arithmetic (round-to-nearest-even, one rounding per operation, exactly as
 // the reference's bf16 operations round)
 // ---------------------------------------------------------------------------------------

@@ -1,17 +1,17 @@
 // B200 (sm_100a) fused sampling / speculative-verification kernels behind the C ABI of
 // include/sonic_b200.h.
 //
-// One launch per call. Each row (singular, top-k) or request (multistep) is cut into S
+// Singular and top-k calls are one launch; a multistep call is two (the rows' streaming
+// pass, then one CTA per request for merge and verification). Each row is cut into S
 // column splits, one 256-thread CTA per split. A CTA streams its split from HBM exactly
-// once: bulk (TMA) copies fill a 3-stage shared-memory ring that is refilled as soon as a
-// stage is consumed, so two chunks are always in flight. Each thread turns 8 columns into
-// processed bf16 logits with packed bf16x2 arithmetic and keeps the ones at or above a
-// rising value threshold: single-row kernels in a sorted per-warp top-128 held in
-// registers (fed through a per-warp shared-memory queue), the multistep kernel in a
-// per-row shared-memory candidate buffer. The split's exact top-128 (or, for greedy
-// rows, its single best key) goes to the workspace, sorted. The last CTA
-// of the row or request (per-unit ticket in the workspace) merges the S sorted lists with
-// warp bitonic merges and runs selection / verification. No second launch, no host sync.
+// once: bulk (TMA) copies of 2048-column chunks fill a shared-memory ring that is refilled
+// as soon as every warp has consumed a stage, so several chunks are always in flight. Each
+// thread turns 8 columns into processed bf16 logits with packed bf16x2 arithmetic and keeps
+// the ones at or above a rising cut in sorted per-warp top-128 lists (fed through per-warp
+// shared-memory queues). The split's exact top-128 (or, for greedy rows, its single best
+// key) goes to the workspace, sorted. The last CTA of a singular or top-k row (per-row
+// ticket in the workspace) merges the S sorted lists with warp bitonic merges and runs the
+// selection. No host sync anywhere.
 //
 // Reference kernels covered (tachyontrails/sonic-sampler, src/sonic_sampler/):
 //   ops/prologue.py:272-472   bitpacked_reduction_kernel (processors + tile candidates)
@@ -38,10 +38,7 @@ namespace sonic {
 constexpr int NT = 256;                    // threads per CTA
 constexpr int VPT = 8;                     // consecutive columns per thread per chunk
 constexpr int CH = NT * VPT;               // columns per chunk (single-row kernels)
-constexpr int CH_MS = 1024;                // columns per chunk (multistep: many rows per CTA)
-constexpr int VPT_MS = CH_MS / NT;         // 4 columns per thread (multistep)
 constexpr int STAGES = 3;                  // bulk-copy ring depth
-constexpr int CAP_MS = 1536;               // candidate keys per row of a multistep CTA
 constexpr int TARGET_CTAS = 296;           // 148 SMs x 2 resident CTAs: one wave
 constexpr int MAX_SPLIT_COLS = 65536;      // local column index fits 16 bits
 constexpr int MAX_SPLITS = 32;
@@ -381,31 +378,8 @@ __device__ __forceinline__ uint32_t load_g8(const SonicSamplingParams& P, int64_
 }
 
 // ---------------------------------------------------------------------------------------
-// shared-memory candidate buffer
+// candidate keys, tickets, list merges and the 128-wide selection steps
 // ---------------------------------------------------------------------------------------
-
-// Append the keys of the set bits of `m` (warp-aggregated atomics). Returns, on every lane,
-// the buffer count right after this warp's append (0 when the warp appended nothing).
-template <typename K>
-__device__ __forceinline__ int cand_push(K* buf, int* cnt, const K (&key)[VPT], unsigned m, int lane) {
-  const int np = __popc(m);
-  int incl = np;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int y = __shfl_up_sync(kFull, incl, d);
-    if (lane >= d) incl += y;
-  }
-  const int total = __shfl_sync(kFull, incl, 31);
-  if (total == 0) return 0;
-  int base = 0;
-  if (lane == 31) base = atomicAdd(cnt, total);
-  base = __shfl_sync(kFull, base, 31);
-  int pos = base + incl - np;
-#pragma unroll
-  for (int j = 0; j < VPT; ++j)
-    if ((m >> j) & 1u) buf[pos++] = key[j];
-  return base + total;
-}
 
 template <typename K>
 __device__ __forceinline__ float key_value(K k);
@@ -413,35 +387,6 @@ template <>
 __device__ __forceinline__ float key_value<uint32_t>(uint32_t k) { return bf2f(dec16(k >> 16)); }
 template <>
 __device__ __forceinline__ float key_value<uint64_t>(uint64_t k) { return dec32((uint32_t)(k >> 32)); }
-
-// Keep exactly the 128 largest keys of buf[0..*cnt) (requires *cnt > 128) and raise the
-// value threshold to the 128th key's value. Block-wide; starts and ends synchronised.
-template <typename K>
-__device__ void cand_compact(K* buf, int* cnt, float* thr, K* top, int* tcnt, int* hist, int* bcast) {
-  const int tid = threadIdx.x, lane = tid & 31;
-  const int n = *cnt;
-  const K T = block_select<K, NT>(buf, n, kMaxK, hist, bcast);
-  if (tid == 0) *tcnt = 0;
-  __syncthreads();
-  for (int base = 0; base < n; base += NT) {
-    const int i = base + tid;
-    const K k = i < n ? buf[i] : (K)0;
-    const bool keep = i < n && k >= T;
-    const unsigned b = __ballot_sync(kFull, keep);
-    int off = 0;
-    if (lane == 0 && b) off = atomicAdd(tcnt, __popc(b));
-    off = __shfl_sync(kFull, off, 0);
-    const int pos = off + __popc(b & ((1u << lane) - 1u));
-    if (keep && pos < kMaxK) top[pos] = k;
-  }
-  __syncthreads();
-  for (int i = tid; i < kMaxK; i += NT) buf[i] = top[i];
-  if (tid == 0) {
-    *cnt = kMaxK;
-    *thr = key_value<K>(T);
-  }
-  __syncthreads();
-}
 
 // local key -> global sortable key ((enc << 32) | ~column); 0 for an empty slot
 template <typename K>
@@ -457,28 +402,6 @@ __device__ __forceinline__ uint64_t to_global<uint64_t>(uint64_t k, int64_t c0) 
   if (k == 0) return 0;
   const int64_t col = c0 + (int64_t)(0xffffffffu - (uint32_t)k);
   return (k & 0xffffffff00000000ull) | (uint64_t)(0xffffffffu - (uint32_t)col);
-}
-
-// Final per-split step: exact top-128 of the buffer, sorted, written as global keys.
-template <typename K>
-__device__ void split_finish(K* buf, int* cnt, float* thr, K* top, int* tcnt, int* hist, int* bcast, int64_t c0,
-                             uint64_t* out) {
-  __syncthreads();
-  if (*cnt > kMaxK) cand_compact<K>(buf, cnt, thr, top, tcnt, hist, bcast);
-  const int n = *cnt;
-  if (threadIdx.x < 32) {
-    const int lane = threadIdx.x;
-    uint64_t k[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = 4 * lane + j;
-      k[j] = i < n ? to_global<K>(buf[i], c0) : 0ull;
-    }
-    warp_sort128_desc(k, lane);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) stcg64(out + 4 * lane + j, k[j]);
-    __threadfence();
-  }
 }
 
 // Ticket: true in the last CTA of the unit to arrive; that CTA also re-arms the ticket.
@@ -922,7 +845,7 @@ __device__ __forceinline__ void row_smem_init(RowSmem<K>& st, unsigned long long
 // Loads of one group of 8 columns per lane (`c` = first column of this lane).
 template <int MODE, bool INDIRECT>
 __device__ __forceinline__ void load_group(const SonicSingularArgs& a, const RowConsts& rc, int64_t slot,
-                                           const uint16_t* xrow, int64_t c, int nvalid, Raw8& raw) {
+                                           int64_t gslot, const uint16_t* xrow, int64_t c, int nvalid, Raw8& raw) {
   constexpr int AM = INDIRECT ? kScalar : MODE;
   load_x8<MODE>(xrow, c, nvalid, raw.x);
   raw.g = 0xffu;
@@ -934,8 +857,38 @@ __device__ __forceinline__ void load_group(const SonicSingularArgs& a, const Row
       if (INDIRECT && j < nvalid) col[j] = load_index(a.d2t, a.d2t_dtype, col[j]);
     }
     load_aux8<AM>(a.params, rc, slot, col, nvalid, raw);
-    if (rc.nd.g) raw.g = load_g8<AM>(a.params, slot, col, nvalid);
+    if (rc.nd.g) raw.g = load_g8<AM>(a.params, gslot, col, nvalid);
   }
+}
+
+// Rows of a multistep call streamed by singular_kernel (MS mode): row r of the flattened
+// logits is step s of request b; request b's steps are rows [margin, margin + T).
+struct MsRows {
+  const int32_t* cu_seqlens;  // varlen: [batch + 1] row offsets, else NULL (T = lookahead + 1)
+  const int32_t* tokens;      // flattened drafted tokens [rows]
+  int32_t batch;
+  int32_t lookahead;
+};
+
+// request and step of multistep row r; false for a row outside every request
+__device__ __forceinline__ bool ms_row(const MsRows& m, int64_t r, int64_t& b, int& s, int64_t& margin) {
+  if (!m.cu_seqlens) {
+    b = r / (m.lookahead + 1);
+    s = (int)(r % (m.lookahead + 1));
+    margin = b * (m.lookahead + 1);
+    return b < m.batch;
+  }
+  int lo = 0, hi = m.batch;  // largest b with cu_seqlens[b] <= r
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (m.cu_seqlens[mid] <= r) lo = mid;
+    else hi = mid;
+  }
+  b = lo;
+  margin = m.cu_seqlens[lo];
+  const int64_t t = m.cu_seqlens[lo + 1] - margin;
+  s = (int)(r - margin);
+  return r >= margin && s < t && s <= m.lookahead;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -1025,9 +978,9 @@ __device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r
 // (ops/prologue.py:272 + ops/singular.py:154)
 // ---------------------------------------------------------------------------------------
 
-template <int MODE, bool INDIRECT>
+template <int MODE, bool INDIRECT, bool MS>
 __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
-                                                      Workspace ws, uint64_t* cand_out) {
+                                                      Workspace ws, uint64_t* cand_out, const MsRows ms) {
   __shared__ __align__(16) RowSmem<uint32_t> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1039,22 +992,30 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   pdl_wait();
 
-  const int64_t slot = load_slot(P, r);
+  // MS: row r is step `step` of multistep request `req` (rows [margin, margin + T))
+  int64_t req = r, margin = 0;
+  int step = 0;
+  if (MS && !ms_row(ms, r, req, step, margin)) return;
+  const int64_t slot = load_slot(P, req);
   if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
     // out-of-range slot id: no CTA of this row touches per-slot buffers or the ticket
-    if (split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
+    if (!MS && split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
     return;
   }
   const uint32_t ind = P.indicators[slot];
   const RowConsts rc = row_consts(P, slot, ind);
   // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
   const bool greedy = (ind & 0x40) != 0 && !cand_out;
-  const int ntok = (a.drafted_tokens && rc.nd.dec) ? a.lookahead : 0;
-  if (tid < ntok) st.toks[tid] = a.drafted_tokens[slot * a.drafted_stride + tid];
+  // drafted tokens counted as decoded: singular counts all `lookahead` drafted tokens of the
+  // slot (ops/prologue.py:175-184); multistep step s counts the request's first s
+  const int ntok = !rc.nd.dec ? 0 : (MS ? step : (a.drafted_tokens ? a.lookahead : 0));
+  if (tid < ntok) st.toks[tid] = MS ? ms.tokens[margin + tid] : a.drafted_tokens[slot * a.drafted_stride + tid];
+  // grammar row: per slot, or per (slot, step) in multistep (ops/prologue.py:29-54)
+  const int64_t gslot = MS ? slot * (ms.lookahead + 1) + step : slot;
   // streams of the bulk-copy ring (see below)
   const int64_t shard = a.shard_offset;
   const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
-  const uint32_t* grow = rc.nd.g ? P.grammar + slot * P.grammar_stride : nullptr;
+  const uint32_t* grow = rc.nd.g ? P.grammar + gslot * P.grammar_stride : nullptr;
   const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
   const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
   const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
@@ -1296,7 +1257,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       }
       if (grow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
     } else {
-      load_group<DM, INDIRECT>(a, rc, slot, xrow, c, nv, raw);
+      load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, c, nv, raw);
     }
     process_group(raw, c, nv, k);
     if (staged) {
@@ -1349,7 +1310,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       tq = false;  // the exact path pushes final keys
       for (int gg = warp; gg < ngroups; gg += NW) {
         Raw8 raw;
-        load_group<DM, INDIRECT>(a, rc, slot, xrow, gcol(gg), gvalid(gg), raw);
+        load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, gcol(gg), gvalid(gg), raw);
         wtk_adopt(w, &st.cut, lane);
         exact_group(raw, gcol(gg), gvalid(gg));
         absorb_if_full();
@@ -1372,6 +1333,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
   }
 
+  if (MS) return;  // multistep rows: ms_verify_kernel merges the lists after this grid
   if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
 
   // ---- merge + selection ----
@@ -1600,60 +1562,26 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
 }
 
 // ---------------------------------------------------------------------------------------
-// fused multistep: prologue over all gamma+1 rows of a request (count and bias rows read
-// once per request), merge per row, softmax of the masked candidates, chain verification
-// (ops/prologue.py:272 + ops/multistep.py:76 + ops/verify.py:244)
+// fused multistep (ops/prologue.py:272 + ops/multistep.py:76 + ops/verify.py:244): the
+// rows of every request stream through singular_kernel in MS mode (per-split top-128
+// lists in the workspace); then one CTA per request merges each row's lists, writes the
+// stage-2 buffers and runs the chain verification
 // ---------------------------------------------------------------------------------------
 
 struct MsSmem {
-  int hist[256];
-  int bcast[4];
-  int cnt[MS_MAX_STEPS];
-  float thr[MS_MAX_STEPS];
-  uint32_t vmin2[MS_MAX_STEPS];
-  int warp_over[2][NT / 32];
-  int tcnt;
-  int flag;
-  int err;
   int32_t drafted[MS_MAX_STEPS];
-  unsigned long long best[MS_MAX_STEPS];
-  uint32_t top[kMaxK];
-  uint64_t bars[STAGES];
-  // after the streaming phase (last CTA only):
   float prob[MS_MAX_STEPS][kMaxK];
   int32_t cand[MS_MAX_STEPS][kMaxK];
   int64_t gsel[MS_MAX_STEPS];
 };
 
-__host__ __device__ constexpr size_t ms_state_bytes() { return (sizeof(MsSmem) + 127) / 128 * 128; }
-
-// stage layout of one 1024-column multistep chunk: aux, then per-row logits + grammar bits
-constexpr int MS_D = 0;
-constexpr int MS_C = MS_D + CH_MS * 4;
-constexpr int MS_B = MS_C + CH_MS * 4;
-constexpr int MS_X = MS_B + CH_MS * 2;
-constexpr int MS_STEP = CH_MS * 2 + 128;
-
-__host__ __device__ inline size_t ms_stage_bytes(int steps) { return (size_t)MS_X + (size_t)steps * MS_STEP; }
-
-static size_t ms_smem_bytes(int steps, int mode) {
-  size_t s = ms_state_bytes() + (size_t)steps * CAP_MS * sizeof(uint32_t);
-  if (mode == kTma) s += STAGES * ms_stage_bytes(steps);
-  return s;
-}
-
-template <int MODE>
-__global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs a, int splits, int cols, int log2bn,
+__global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs a, int splits, int log2bn,
                                                        Workspace ws) {
-  extern __shared__ __align__(128) unsigned char smem_raw[];
-  MsSmem& sm = *reinterpret_cast<MsSmem*>(smem_raw);
+  __shared__ __align__(16) MsSmem sm;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int split = blockIdx.x;
-  const int64_t b = blockIdx.y;
+  const int64_t b = blockIdx.x;
   const SonicSamplingParams& P = a.params;
   const int G = a.lookahead;
-  const int64_t c0 = (int64_t)split * cols;
-  const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
 
   pdl_wait();
 
@@ -1669,331 +1597,13 @@ __global__ void __launch_bounds__(NT) multistep_kernel(const SonicMultistepArgs 
   T = max((int64_t)1, min(T, (int64_t)(G + 1)));
   const int64_t slot = load_slot(P, b);
   if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots) || margin < 0 || margin + T > a.total_rows) {
-    if (split == 0 && tid == 0) a.offsets[b] = -1;
+    if (tid == 0) a.offsets[b] = -1;
     return;
   }
   const uint32_t ind = P.indicators[slot];
-  const RowConsts rc = row_consts(P, slot, ind);
   const bool greedy = (ind & 0x40) != 0;
-  uint32_t* bufs = reinterpret_cast<uint32_t*>(smem_raw + ms_state_bytes());
-  unsigned char* stages = reinterpret_cast<unsigned char*>(bufs + (size_t)(G + 1) * CAP_MS);
-  const size_t stage_bytes = ms_stage_bytes(G + 1);
-  if (tid < T) {
-    sm.drafted[tid] = a.drafted_tokens[margin + tid];
-    sm.cnt[tid] = 0;
-    sm.thr[tid] = kFiniteFloor;
-    sm.vmin2[tid] = rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u;
-    sm.best[tid] = 0ull;
-  }
-  if (tid == 0) {
-    sm.err = 0;
-    if (MODE == kTma) {
-      for (int s = 0; s < STAGES; ++s) mbar_init(&sm.bars[s], 1);
-      mbar_fence_init();
-    }
-  }
+  if (tid < T) sm.drafted[tid] = a.drafted_tokens[margin + tid];
   __syncthreads();
-
-  const int64_t shard = a.shard_offset;
-  const int64_t grow0 = slot * (G + 1);
-  uint32_t compacted = 0;  // bit s: row s had its first compaction (uniform across threads)
-  int parity = 0;
-
-  // process VPT_MS columns [c, c + VPT_MS) of every row of the request; returns the rows
-  // whose buffer count passed its compaction limit (this thread's view)
-  auto consume_rows = [&](int64_t c, int nvalid, const int32_t (&d)[VPT_MS], const int32_t (&cx)[VPT_MS],
-                          const uint32_t (&bb)[VPT_MS / 2], auto&& get_x, auto&& get_g) -> int {
-    int over = 0;
-    for (int s = 0; s < T; ++s) {
-      uint32_t xw[VPT_MS / 2];
-      get_x(s, xw);
-      const uint32_t g = rc.nd.g ? get_g(s) : 0xffu;
-      if (rc.nd.proc || rc.nd.temp) {
-#pragma unroll
-        for (int p = 0; p < VPT_MS / 2; ++p) {
-          int32_t d0 = d[2 * p], d1 = d[2 * p + 1];
-          if (rc.nd.dec)
-            for (int q = 0; q < s; ++q) {
-              d0 += (sm.drafted[q] == c + 2 * p + shard);
-              d1 += (sm.drafted[q] == c + 2 * p + 1 + shard);
-            }
-          xw[p] = process_pair(xw[p], (g >> (2 * p)) & 3u, d0, d1, cx[2 * p], cx[2 * p + 1], bb[p], rc);
-        }
-      }
-      if (greedy) {
-        uint64_t best = 0;
-#pragma unroll
-        for (int j = 0; j < VPT_MS; ++j)
-          if (j < nvalid) best = umax(best, greedy_key_bits(half_of(xw, j), c + j, log2bn));
-        best = warp_max_u64(best);
-        if (lane == 0 && best) atomicMax(&sm.best[s], (unsigned long long)best);
-      } else {
-        const float thr = sm.thr[s];
-        uint32_t key[VPT];
-        unsigned m = 0;
-#pragma unroll
-        for (int j = 0; j < VPT; ++j) {
-          key[j] = 0;
-          if (j < VPT_MS) {
-            const uint32_t h = half_of(xw, j);
-            key[j] = (enc16(h) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
-            if (j < nvalid && bf2f((uint16_t)h) >= thr) m |= 1u << j;
-          }
-        }
-        const int end = cand_push<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], key, m, lane);
-        const int lim = ((compacted >> s) & 1u) ? CAP_MS - CH_MS : kMaxK;
-        if (end > lim) over |= 1 << s;
-      }
-    }
-    return over;
-  };
-
-  // block-wide OR of the per-thread masks; one barrier (double-buffered warp slots)
-  auto block_or = [&](int over) -> int {
-    const int v = (int)__reduce_or_sync(kFull, (unsigned)over);
-    if (lane == 0) sm.warp_over[parity][warp] = v;
-    __syncthreads();
-    int res = 0;
-#pragma unroll
-    for (int w = 0; w < NT / 32; ++w) res |= sm.warp_over[parity][w];
-    parity ^= 1;
-    return res;
-  };
-
-  auto compact_rows = [&](int full) {
-    for (int s = 0; s < T; ++s)
-      if ((full >> s) & 1) {
-        cand_compact<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt, sm.hist,
-                               sm.bcast);
-        if (tid == 0 && rc.fast) sm.vmin2[s] = vmin_pair(sm.thr[s], rc);
-      }
-    compacted |= (uint32_t)full;
-    if (rc.fast) __syncthreads();
-  };
-
-  // fast path (see vmin_pair): one thread's 4 columns of every row straight from the stage
-  auto fast_rows = [&](unsigned char* sp, int64_t c) -> int {
-    const int32_t* sd = reinterpret_cast<const int32_t*>(sp + MS_D) + VPT_MS * tid;
-    const int32_t* sc = reinterpret_cast<const int32_t*>(sp + MS_C) + VPT_MS * tid;
-    uint32_t base_need = 0;
-    if (rc.nd.dec) {
-      const uint4 d4 = *reinterpret_cast<const uint4*>(sd);
-      uint32_t nz[VPT_MS] = {d4.x, d4.y, d4.z, d4.w};
-      if (rc.nd.ctx) {
-        const uint4 c4 = *reinterpret_cast<const uint4*>(sc);
-        nz[0] |= c4.x; nz[1] |= c4.y; nz[2] |= c4.z; nz[3] |= c4.w;
-      }
-#pragma unroll
-      for (int j = 0; j < VPT_MS; ++j) base_need |= (uint32_t)(nz[j] != 0u) << j;
-    }
-    uint2 bq = make_uint2(0u, 0u);
-    if (rc.nd.bias) bq = *reinterpret_cast<const uint2*>(sp + MS_B + 8 * tid);
-    int over = 0;
-    for (int s = 0; s < T; ++s) {
-      unsigned char* row = sp + MS_X + s * MS_STEP;
-      uint32_t* sx = reinterpret_cast<uint32_t*>(row) + 2 * tid;
-      if (rc.nd.dec) {
-        uint32_t need = base_need;
-        for (int q = 0; q < s; ++q) {
-          const int64_t dl = (int64_t)sm.drafted[q] - (c + shard);
-          if (dl >= 0 && dl < VPT_MS) need |= 1u << dl;
-        }
-        while (need) {
-          const int j = __ffs(need) - 1;
-          need &= need - 1;
-          int32_t dj = sd[j];
-          for (int q = 0; q < s; ++q) dj += (sm.drafted[q] == c + j + shard);
-          uint16_t* xp = reinterpret_cast<uint16_t*>(sx) + j;
-          *xp = (uint16_t)repetition_one(*xp, dj, rc.nd.ctx ? sc[j] : 0, rc);
-        }
-      }
-      const uint2 xq = *reinterpret_cast<const uint2*>(sx);
-      uint32_t x[2] = {xq.x, xq.y};
-      if (rc.nd.bias) {
-        x[0] = bf2_add(x[0], bq.x);
-        x[1] = bf2_add(x[1], bq.y);
-      }
-      uint32_t m = ge_mask4(x, sm.vmin2[s]);
-      if (rc.nd.g) m &= (uint32_t)(row[CH_MS * 2 + (tid >> 1)] >> (4 * (tid & 1)));
-      int end = 0;
-      if (m) {
-        *reinterpret_cast<uint2*>(sx) = make_uint2(x[0], x[1]);
-        while (m) {
-          const int j = __ffs(m) - 1;
-          m &= m - 1;
-          const float fv = final_value(bf2f(reinterpret_cast<const uint16_t*>(sx)[j]), rc);
-          if (fv == fv && fabsf(fv) <= 3.3895313892515355e+38f) {
-            const uint32_t key = (enc16(f2bf(fv)) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
-            const int pos = atomicAdd(&sm.cnt[s], 1);
-            if (pos < CAP_MS) bufs[(size_t)s * CAP_MS + pos] = key;
-            end = pos + 1;
-          }
-        }
-      }
-      const int lim = ((compacted >> s) & 1u) ? CAP_MS - CH_MS : kMaxK;
-      if (end > lim) over |= 1 << s;
-    }
-    return over;
-  };
-
-  auto direct_chunk = [&](int64_t cb) -> int {
-    constexpr int DM = (MODE == kTma) ? kVec : MODE;
-    const int64_t c = cb + (int64_t)VPT_MS * tid;
-    const int nvalid = (int)max((int64_t)0, min((int64_t)VPT_MS, c1 - c));
-    int32_t d[VPT_MS] = {0, 0, 0, 0}, cx[VPT_MS] = {0, 0, 0, 0};
-    uint32_t bb[VPT_MS / 2] = {0, 0};
-    if (rc.nd.proc) {
-#pragma unroll
-      for (int j = 0; j < VPT_MS; ++j) {
-        const bool ok = j < nvalid;
-        const int64_t col = c + j + shard;
-        if (rc.nd.dec && ok) d[j] = __ldcs(P.decode_counts + slot * P.counts_stride + col);
-        if (rc.nd.ctx && ok) cx[j] = __ldcs(P.context_counts + slot * P.counts_stride + col);
-        if (rc.nd.bias && ok) bb[j >> 1] |= (uint32_t)__ldcs(P.bias + slot * P.bias_stride + col) << (16 * (j & 1));
-      }
-    }
-    auto get_x = [&](int s, uint32_t (&xw)[VPT_MS / 2]) {
-      const uint16_t* xr = (const uint16_t*)a.logits + (margin + s) * a.logits_stride;
-      if (DM == kVec && nvalid == VPT_MS) {
-        const uint2 q = __ldcs(reinterpret_cast<const uint2*>(xr + c));
-        xw[0] = q.x;
-        xw[1] = q.y;
-      } else {
-#pragma unroll
-        for (int p = 0; p < VPT_MS / 2; ++p) {
-          const uint32_t lo = (2 * p < nvalid) ? (uint32_t)__ldcs(xr + c + 2 * p) : 0xff80u;
-          const uint32_t hi = (2 * p + 1 < nvalid) ? (uint32_t)__ldcs(xr + c + 2 * p + 1) : 0xff80u;
-          xw[p] = lo | (hi << 16);
-        }
-      }
-    };
-    auto get_g = [&](int s) -> uint32_t {
-      const uint32_t* g = P.grammar + (grow0 + s) * P.grammar_stride;
-      uint32_t bits = 0;
-#pragma unroll
-      for (int j = 0; j < VPT_MS; ++j)
-        if (j < nvalid) bits |= ((__ldg(g + ((c + j + shard) >> 5)) >> ((c + j + shard) & 31)) & 1u) << j;
-      return bits;
-    };
-    return consume_rows(c, nvalid, d, cx, bb, get_x, get_g);
-  };
-
-  int64_t cb = c0;
-  if (MODE == kTma) {
-    const int nfull = (int)((c1 - c0) / CH_MS);
-    const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
-    const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
-    const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
-    const uint32_t tx = (drow ? CH_MS * 4 : 0) + (crow ? CH_MS * 4 : 0) + (brow ? CH_MS * 2 : 0) +
-                        (uint32_t)T * (CH_MS * 2 + (rc.nd.g ? CH_MS / 8 : 0));
-    auto issue = [&](int i) {
-      unsigned char* sp = stages + (size_t)(i % STAGES) * stage_bytes;
-      uint64_t* bar = &sm.bars[i % STAGES];
-      const int64_t cc = c0 + (int64_t)i * CH_MS;
-      mbar_expect_tx(bar, tx);
-      if (drow) bulk_load(sp + MS_D, drow + cc + shard, CH_MS * 4, bar);
-      if (crow) bulk_load(sp + MS_C, crow + cc + shard, CH_MS * 4, bar);
-      if (brow) bulk_load(sp + MS_B, brow + cc + shard, CH_MS * 2, bar);
-      for (int s = 0; s < T; ++s) {
-        const uint16_t* xr = (const uint16_t*)a.logits + (margin + s) * a.logits_stride;
-        bulk_load(sp + MS_X + s * MS_STEP, xr + cc, CH_MS * 2, bar);
-        if (rc.nd.g)
-          bulk_load(sp + MS_X + s * MS_STEP + CH_MS * 2,
-                    P.grammar + (grow0 + s) * P.grammar_stride + (cc + shard) / 32, CH_MS / 8, bar);
-      }
-    };
-    if (tid == 0)
-      for (int i = 0; i < min(nfull, STAGES); ++i) issue(i);
-    for (int i = 0; i < nfull; ++i) {
-      const unsigned char* sp = stages + (size_t)(i % STAGES) * stage_bytes;
-      if (!sm.err && !mbar_wait_bounded(&sm.bars[i % STAGES], (uint32_t)(i / STAGES) & 1u, WAIT_LIMIT)) sm.err = 1;
-      const int64_t c = cb + (int64_t)VPT_MS * tid;
-      if (rc.fast) {
-        const int full = block_or(fast_rows(const_cast<unsigned char*>(sp), c));
-        if (tid == 0 && i + STAGES < nfull) {
-          fence_proxy_async();
-          issue(i + STAGES);
-        }
-        if (full) compact_rows(full);
-        cb += CH_MS;
-        continue;
-      }
-      int32_t d[VPT_MS] = {0, 0, 0, 0}, cx[VPT_MS] = {0, 0, 0, 0};
-      uint32_t bb[VPT_MS / 2] = {0, 0};
-      if (rc.nd.dec) {
-        const uint4 q = *reinterpret_cast<const uint4*>(sp + MS_D + tid * 16);
-        d[0] = q.x; d[1] = q.y; d[2] = q.z; d[3] = q.w;
-      }
-      if (rc.nd.ctx) {
-        const uint4 q = *reinterpret_cast<const uint4*>(sp + MS_C + tid * 16);
-        cx[0] = q.x; cx[1] = q.y; cx[2] = q.z; cx[3] = q.w;
-      }
-      if (rc.nd.bias) {
-        const uint2 q = *reinterpret_cast<const uint2*>(sp + MS_B + tid * 8);
-        bb[0] = q.x;
-        bb[1] = q.y;
-      }
-      auto get_x = [&](int s, uint32_t (&xw)[VPT_MS / 2]) {
-        const uint2 q = *reinterpret_cast<const uint2*>(sp + MS_X + s * MS_STEP + tid * 8);
-        xw[0] = q.x;
-        xw[1] = q.y;
-      };
-      auto get_g = [&](int s) -> uint32_t {
-        // thread t's 4 columns are bits 4(t & 1) .. 4(t & 1) + 3 of grammar byte t / 2
-        const uint32_t byte = sp[MS_X + s * MS_STEP + CH_MS * 2 + (tid >> 1)];
-        return (byte >> (4 * (tid & 1))) & 0xfu;
-      };
-      const int full = block_or(consume_rows(c, VPT_MS, d, cx, bb, get_x, get_g));
-      if (tid == 0 && i + STAGES < nfull) {
-        fence_proxy_async();
-        issue(i + STAGES);
-      }
-      if (!greedy && full) compact_rows(full);
-      cb += CH_MS;
-    }
-  }
-  for (; cb < c1; cb += CH_MS) {
-    const int full = block_or(direct_chunk(cb));
-    if (!greedy && full) compact_rows(full);
-  }
-  // rows with fewer than 128 finite candidates in this split: redo them keeping -inf
-  if (!greedy) {
-    __syncthreads();
-    int redo = 0;
-    for (int s = 0; s < T; ++s)
-      if (sm.cnt[s] < kMaxK) redo |= 1 << s;
-    __syncthreads();
-    if (redo) {
-      if (tid < T) {
-        sm.cnt[tid] = 0;
-        sm.thr[tid] = __int_as_float(0xff800000);
-      }
-      compacted = 0xffffffffu;
-      __syncthreads();
-      for (int64_t cc = c0; cc < c1; cc += CH_MS) {
-        const int full = block_or(direct_chunk(cc));
-        if (full) compact_rows(full);
-      }
-    }
-  }
-  pdl_trigger();
-  __syncthreads();
-  if (sm.err) {
-    if (tid == 0) atomicOr(ws.error, 1u);
-    return;
-  }
-
-  if (greedy) {
-    if (tid < T) {
-      stcg64(ws.cand + ((margin + tid) * splits + split) * kMaxK, sm.best[tid]);
-      __threadfence();
-    }
-  } else {
-    for (int s = 0; s < T; ++s)
-      split_finish<uint32_t>(bufs + (size_t)s * CAP_MS, &sm.cnt[s], &sm.thr[s], sm.top, &sm.tcnt, sm.hist, sm.bcast,
-                             c0, ws.cand + ((margin + s) * splits + split) * kMaxK);
-  }
-  if (!arrive_last(ws.tickets + b, splits, &sm.flag)) return;
 
   // ---- per-row merge (warp w handles rows w, w+8, ...) ----
   for (int s = warp; s < T; s += NT / 32) {
@@ -2213,7 +1823,7 @@ static sonic_status check_params(const SonicSamplingParams& P) {
 }
 
 static Plan singular_plan(int64_t rows, int64_t V) { return split_plan(rows, V, CH); }
-static Plan multistep_plan(int64_t batch, int64_t V) { return split_plan(batch, V, CH_MS); }
+static Plan multistep_plan(int64_t rows, int64_t V) { return split_plan(rows, V, CH); }
 
 static int64_t multistep_rows(const SonicMultistepArgs* a) {
   return a->total_rows > 0 ? a->total_rows : (int64_t)a->batch_size * (a->lookahead + 1);
@@ -2236,7 +1846,7 @@ size_t sonic_fused_singular_workspace_size(const SonicSingularArgs* a) {
 
 size_t sonic_fused_multistep_workspace_size(const SonicMultistepArgs* a) {
   if (!a || a->batch_size <= 0) return 0;
-  return workspace_bytes(multistep_rows(a), a->batch_size, multistep_plan(a->batch_size, a->vocab_size).splits);
+  return workspace_bytes(multistep_rows(a), a->batch_size, multistep_plan(multistep_rows(a), a->vocab_size).splits);
 }
 
 size_t sonic_bounded_topk_workspace_size(const SonicTopKArgs* a) {
@@ -2295,13 +1905,13 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   const size_t ring = mode == kTma ? (size_t)RING_BYTES : 0;
   cudaError_t e;
   if (ind)
-    e = mode == kVec ? launch(singular_kernel<kVec, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand)
-                     : launch(singular_kernel<kScalar, true>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
+    e = mode == kVec ? launch(singular_kernel<kVec, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
+                     : launch(singular_kernel<kScalar, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
   else if (mode == kTma)
-    e = launch(singular_kernel<kTma, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
+    e = launch(singular_kernel<kTma, false, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
   else
-    e = mode == kVec ? launch(singular_kernel<kVec, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand)
-                     : launch(singular_kernel<kScalar, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand);
+    e = mode == kVec ? launch(singular_kernel<kVec, false, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
+                     : launch(singular_kernel<kScalar, false, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
   return check_launch(e, what);
 }
 
@@ -2394,30 +2004,45 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "max_top_logprobs must be in [0, 128]");
   if (a->logprobs_dtype != SONIC_DTYPE_BF16 && a->logprobs_dtype != SONIC_DTYPE_F32)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logprobs dtype must be bf16 or f32");
-  const Plan p = multistep_plan(a->batch_size, a->vocab_size);
   const int64_t rows = multistep_rows(a);
+  if (rows > 65535) return fail(SONIC_ERR_INVALID_ARGUMENT, "multistep rows (batch x steps) must be <= 65535");
+  const Plan p = multistep_plan(rows, a->vocab_size);
   const size_t need = workspace_bytes(rows, a->batch_size, p.splits);
   if (!a->workspace || a->workspace_bytes < need)
     return fail(SONIC_ERR_WORKSPACE, "workspace smaller than sonic_fused_multistep_workspace_size()");
   const Workspace ws = carve(a->workspace, rows, a->batch_size, p.splits);
+  // the rows stream through the singular kernel (MS mode), which reads these fields only
+  SonicSingularArgs sa;
+  memset(&sa, 0, sizeof(sa));
+  sa.rows = (int32_t)rows;
+  sa.vocab_size = a->vocab_size;
+  sa.block_n = a->block_n;
+  sa.shard_offset = a->shard_offset;
+  sa.flags = a->flags & SONIC_FLAG_PDL;
+  sa.logits = a->logits;
+  sa.logits_dtype = a->logits_dtype;
+  sa.logits_stride = a->logits_stride;
+  sa.params = a->params;
+  sa.tokens = a->tokens;
+  const MsRows m{a->cu_seqlens, a->drafted_tokens, a->batch_size, a->lookahead};
   const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
-  const int steps = a->lookahead + 1;
-  int mode = kScalar;
-  if (xvec && params_vec_ok(a->params, a->shard_offset)) mode = kVec;
-  if (mode == kVec && params_tma_ok(a->params, a->shard_offset) && ms_smem_bytes(steps, kTma) <= 200 * 1024)
-    mode = kTma;
-  const size_t smem = ms_smem_bytes(steps, mode);
-  dim3 grid(p.splits, a->batch_size);
+  int mode = (xvec && params_vec_ok(a->params, a->shard_offset)) ? kVec : kScalar;
+  if (mode == kVec && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
+  const dim3 grid(p.splits, (unsigned)rows);
   cudaError_t e;
   if (mode == kTma)
-    e = launch(multistep_kernel<kTma>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
+    e = launch(singular_kernel<kTma, false, true>, grid, (size_t)RING_BYTES, st, pdl, sa, p.splits, p.cols, l2, ws,
+               (uint64_t*)nullptr, m);
   else if (mode == kVec)
-    e = launch(multistep_kernel<kVec>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
+    e = launch(singular_kernel<kVec, false, true>, grid, 0, st, pdl, sa, p.splits, p.cols, l2, ws, (uint64_t*)nullptr, m);
   else
-    e = launch(multistep_kernel<kScalar>, grid, smem, st, pdl, *a, p.splits, p.cols, l2, ws);
+    e = launch(singular_kernel<kScalar, false, true>, grid, 0, st, pdl, sa, p.splits, p.cols, l2, ws,
+               (uint64_t*)nullptr, m);
+  if (sonic_status s = check_launch(e, "sonic_fused_multistep (rows)")) return s;
+  e = launch(ms_verify_kernel, dim3(a->batch_size), 0, st, pdl, *a, p.splits, l2, ws);
   return check_launch(e, "sonic_fused_multistep");
 }
 
