@@ -1187,9 +1187,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   // chunk k (full 2048-column chunks only) is group k * NW + warp of every warp
   const int nchunks = MODE == kTma ? (int)((c1 - c0) / CH) : 0;
   bool werr = false;
-  if (MODE == kTma && rc.fast && !greedy && nchunks > 0 && ntok == 0) {
+  if (MODE == kTma && rc.fast && !greedy && nchunks > 0) {
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
-    // columns whose counts are zero (their value needs no penalty), bound 128 distinct keys.
+    // columns whose counts are zero and that hold no drafted token (their value needs no
+    // penalty), bound 128 distinct keys.
     if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
     const uint4 xq = *reinterpret_cast<const uint4*>(smem_ring + warp * (GROUP * 2) + lane * 16);
     uint32_t y[4] = {xq.x, xq.y, xq.z, xq.w};
@@ -1207,6 +1208,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 #pragma unroll
       for (int j = 0; j < VPT; ++j)
         if ((dp[j] | (crow ? cp[j] : 0)) != 0) ok &= ~(1u << j);
+    }
+    for (int t = 0; t < ntok; ++t) {
+      const int64_t dl = (int64_t)st.toks[t] - (gcol(warp) + shard);
+      if (dl >= 0 && dl < VPT) ok &= ~(1u << dl);
     }
     const uint32_t base = (uint32_t)(0xffff - (int)(gcol(warp) - c0));
     uint32_t lm = 0;
@@ -1570,6 +1575,8 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
 
 struct MsSmem {
   int32_t drafted[MS_MAX_STEPS];
+  float u[MS_MAX_STEPS];   // acceptance uniform of each step
+  float qd[MS_MAX_STEPS];  // draft probability of each drafted token (stochastic drafts)
   float prob[MS_MAX_STEPS][kMaxK];
   int32_t cand[MS_MAX_STEPS][kMaxK];
   int64_t gsel[MS_MAX_STEPS];
@@ -1602,7 +1609,22 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   }
   const uint32_t ind = P.indicators[slot];
   const bool greedy = (ind & 0x40) != 0;
-  if (tid < T) sm.drafted[tid] = a.drafted_tokens[margin + tid];
+  const bool stochastic_q = a.draft_probs && !(ind & 0x800) && !greedy;
+  if (tid < T) {
+    const int32_t d = a.drafted_tokens[margin + tid];
+    sm.drafted[tid] = d;
+    // the acceptance loop's per-step inputs, loaded once and in parallel
+    if (!greedy && tid < T - 1) {
+      sm.u[tid] = bf2f(a.uniform[slot * a.uniform_stride + tid]);
+      float q = 1.0f;
+      if (stochastic_q && d >= 0 && d < a.vocab_size) {
+        const int64_t qi = slot * a.draft_stride + tid * a.draft_step_stride + d;
+        q = a.draft_dtype == SONIC_DTYPE_F32 ? ((const float*)a.draft_probs)[qi]
+                                             : bf2f(((const uint16_t*)a.draft_probs)[qi]);
+      }
+      sm.qd[tid] = q;
+    }
+  }
   __syncthreads();
 
   // ---- per-row merge (warp w handles rows w, w+8, ...) ----
@@ -1623,6 +1645,17 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       float v[4];
       int64_t idx[4];
       decode_keys(k, v, idx);
+      // warm L2 with what the rejection step may gather for these candidates
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (idx[j] < 0 || idx[j] >= a.vocab_size) continue;
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + s * a.gumbel_step_stride + idx[j]));
+        if (stochastic_q && s < T - 1) {
+          const int64_t qi = slot * a.draft_stride + s * a.draft_step_stride + idx[j];
+          asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.draft_probs +
+                                                         qi * (a.draft_dtype == SONIC_DTYPE_F32 ? 4 : 2)));
+        }
+      }
       const float vmax = __shfl_sync(kFull, v[0], 0);
       float ev[4];
       if (ind & 0x380) warp_masking(load_mask_params(P, slot), ind, v, vmax, lane, ev);
@@ -1672,13 +1705,12 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
     }
     const bool stochastic_draft = a.draft_probs && !(ind & 0x800);
     for (accepted = 0; accepted < T - 1; ++accepted) {
-      float u = bf2f(a.uniform[slot * a.uniform_stride + accepted]);
+      float u = sm.u[accepted];
       if (stochastic_draft && dr[accepted] >= 0 && dr[accepted] < a.vocab_size) {
-        const int64_t qi = slot * a.draft_stride + accepted * a.draft_step_stride + dr[accepted];
         if (a.draft_dtype == SONIC_DTYPE_F32)
-          u = __fmul_rn(u, ((const float*)a.draft_probs)[qi]);
+          u = __fmul_rn(u, sm.qd[accepted]);
         else
-          u = rbf(__fmul_rn(u, bf2f(((const uint16_t*)a.draft_probs)[qi])));
+          u = rbf(__fmul_rn(u, sm.qd[accepted]));
       }
       bool keep = false;
 #pragma unroll

@@ -435,3 +435,33 @@ def test_multistep_greedy_mixed_bf16_logprobs(dev):
                                      update_counts=True, return_logprobs=True, max_top_logprobs=3, **kw)
     margins = [i * (gamma + 1) for i in range(batch)]
     _verify_logprobs_equal(ver, ref, kh["indicators"], sm.cpu().tolist(), margins)
+
+
+def test_multistep_ragged_vocab_long_lookahead(dev):
+    """Multistep rows on the scalar path (vocabulary not a multiple of 8) with the longest
+    lookahead: every step counts the drafted tokens before it."""
+    gamma, vocab, batch = 15, 32001, 3
+    b = workloads.sampling_buffers(batch, gamma + 1, vocab, dev, 21, workloads.config2_params(batch, 22),
+                                   top_logprobs=2)
+    x = workloads.peaked_logits(batch * (gamma + 1), vocab, sigma=3.0, peaks=4, lift=12.0, device=dev,
+                                seed=23).view(batch, gamma + 1, vocab)
+    tokens = x.float().argmax(-1).to(I32).contiguous()  # drafts the target likes: long accepts
+    kw = buffer_kwargs(b, timestep=None)
+    ver, ref, kw, kh = run_multistep(x, tokens, lookahead=gamma, block_n=4096, update_counts=True,
+                                     return_logprobs=True, max_top_logprobs=2, **kw)
+    _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(batch)), [i * (gamma + 1) for i in range(batch)])
+
+
+def test_multistep_varlen_single_row_requests(dev):
+    """Varlen requests of one row (only the bonus token) next to full-length ones."""
+    gamma, vocab, batch = 4, 128256, 6
+    lengths = [1, 5, 1, 3, 5, 2]
+    cu = torch.tensor([0] + list(torch.tensor(lengths).cumsum(0)), dtype=I32)
+    rows = int(cu[-1])
+    b = workloads.sampling_buffers(batch, gamma + 1, vocab, dev, 31, workloads.config2_params(batch, 32))
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=33)
+    tokens = torch.randint(0, vocab, (rows,), generator=torch.Generator().manual_seed(34)).to(I32).to(dev)
+    kw = buffer_kwargs(b, timestep=None)
+    ver, ref, kw, kh = run_multistep(x, tokens, cu_seqlens=cu.to(dev), lookahead=gamma, block_n=4096,
+                                     update_counts=True, return_logprobs=True, **kw)
+    _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(batch)), cu[:-1].tolist())
