@@ -770,10 +770,11 @@ __device__ __forceinline__ uint32_t vmin_pair(float thr, const RowConsts& rc) {
   return vmin_pair(thr, rc.nd.temp, rc.temp_fast, rc.temp, rc.rtemp);
 }
 
-// Shared-memory state of a single-row CTA.
-template <typename K>
+// Shared-memory state of a single-row CTA; QC is the queue capacity of a warp (at least 127
+// plus the most keys a warp group can push).
+template <typename K, int QC = QCAP>
 struct RowSmem {
-  K queue[NW][QCAP];
+  K queue[NW][QC];
   K lists[NW][kMaxK];
   unsigned long long cut;  // packed CTA cut, see pack_cut
   float v16[NW];           // each warp's 16th kept key value (-inf while it keeps fewer)
@@ -836,8 +837,8 @@ __device__ __forceinline__ uint32_t select4(const uint32_t (&v)[4], int i) {
   return i < 2 ? (i == 0 ? v[0] : v[1]) : (i == 2 ? v[2] : v[3]);
 }
 
-template <typename K>
-__device__ __forceinline__ void row_smem_init(RowSmem<K>& st, unsigned long long cut0) {
+template <typename K, int QC>
+__device__ __forceinline__ void row_smem_init(RowSmem<K, QC>& st, unsigned long long cut0) {
   st.cut = cut0;
   for (int i = 0; i < NW; ++i) st.v16[i] = st.vlm[i] = __int_as_float(0xff800000);
 }
@@ -1375,6 +1376,270 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
     return;
   }
+  select_row(a, r, slot, ind, st.mp, k, lane);
+}
+
+// ---------------------------------------------------------------------------------------
+// plain singular rows: no grammar, counts, bias, d2t or drafted tokens anywhere in the call
+// (logits, optional temperature, then the usual masking and selection). Same machinery as
+// singular_kernel with wider groups: 16 columns a lane, 512 a warp, 4096-column chunks of
+// logits only (8 KB a stage, 9 stages in the ring).
+// ---------------------------------------------------------------------------------------
+
+constexpr int PVPT = 16;               // columns per lane
+constexpr int PGROUP = PVPT * 32;      // columns per warp group
+constexpr int PCH = PGROUP * NW;       // columns per chunk
+constexpr int PSTAGE = PCH * 2;        // bytes per stage
+constexpr int PNST = RING_BYTES / PSTAGE < MAX_RING_STAGES ? RING_BYTES / PSTAGE : MAX_RING_STAGES;
+constexpr int PQCAP = kMaxK + PGROUP;  // a warp appends at most 512 keys per group
+
+// 16 logits of one lane, pre-temperature bf16 pairs; `nvalid` columns valid (-inf beyond)
+template <int MODE>
+__device__ __forceinline__ void load_x16(const uint16_t* xrow, int64_t c, int nvalid, uint32_t (&x)[8]) {
+  uint32_t lo[4], hi[4];
+  load_x8<MODE>(xrow, c, min(nvalid, 8), lo);
+  load_x8<MODE>(xrow, c + 8, max(nvalid - 8, 0), hi);
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    x[p] = lo[p];
+    x[4 + p] = hi[p];
+  }
+}
+
+// half j of x (a runtime j: explicit selects keep x in registers)
+__device__ __forceinline__ uint32_t half16(const uint32_t (&x)[8], int j) {
+  const int i = j >> 1;
+  const uint32_t a = i & 1 ? x[1] : x[0], b = i & 1 ? x[3] : x[2], c = i & 1 ? x[5] : x[4], d = i & 1 ? x[7] : x[6];
+  const uint32_t e = i & 2 ? b : a, f = i & 2 ? d : c;
+  const uint32_t w = i & 4 ? f : e;
+  return (j & 1) ? (w >> 16) : (w & 0xffffu);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
+                                                   Workspace ws) {
+  __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
+  extern __shared__ __align__(128) unsigned char smem_ring[];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int split = blockIdx.x;
+  const int64_t r = blockIdx.y;
+  const SonicSamplingParams& P = a.params;
+  const int64_t c0 = (int64_t)split * cols;
+  const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
+
+  pdl_wait();
+
+  const int64_t slot = load_slot(P, r);
+  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
+    if (split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
+    return;
+  }
+  const uint32_t ind = P.indicators[slot];
+  const RowConsts rc = row_consts(P, slot, ind);
+  const bool greedy = (ind & 0x40) != 0;
+  const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
+  const int nchunks = MODE == kTma ? (int)((c1 - c0) / PCH) : 0;
+  auto issue_chunk = [&](int i, int stage) {  // one thread
+    uint64_t* bar = &st.bars[stage];
+    mbar_expect_tx(bar, (uint32_t)PSTAGE);
+    bulk_load(smem_ring + stage * PSTAGE, xrow + c0 + (int64_t)i * PCH, PSTAGE, bar);
+  };
+  if (tid == 0) {
+    st.best = 0ull;
+    st.mp = load_mask_params(P, slot);
+    row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
+    if (MODE == kTma) {
+      for (int i = 0; i < PNST; ++i) {
+        mbar_init(&st.bars[i], 1);
+        st.rel[i] = 0;
+      }
+      mbar_fence_init();
+      for (int i = 0; i < min(nchunks, PNST); ++i) issue_chunk(i, i);
+    }
+  }
+  __syncthreads();
+
+  uint32_t* q = st.queue[warp];
+  WarpTopK<uint32_t> w;
+  wtk_init(w, st.lists[warp], kFiniteFloor, lane);
+  uint64_t best = 0;
+  bool tq = rc.fast && rc.nd.temp;  // fast-path queues hold pre-temperature keys
+  auto final_of = [&](float v) { return final_value(v, rc); };
+
+  auto absorb_if_full = [&]() {
+    if (w.qn >= kMaxK) {
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp), st.v16, warp, lane);
+      if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
+    }
+  };
+  // queue the keys of the set bits of m (16 columns starting at c)
+  auto push16 = [&](const uint32_t (&y)[8], uint32_t m, int64_t c, bool tempered) {
+    int excl;
+    const int total = warp_offsets(__popc(m), lane, excl);
+    int pos = w.qn + excl;
+    const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
+    while (m) {
+      const int j = __ffs(m) - 1;
+      m &= m - 1;
+      uint32_t h = half16(y, j);
+      if (tempered) h = f2bf(final_value(bf2f((uint16_t)h), rc));
+      q[pos++] = (enc16(h) << 16) | (base - (uint32_t)j);
+    }
+    w.qn += total;
+  };
+  auto process16 = [&](const uint32_t (&x)[8], int64_t c, int nvalid, bool exact) {
+    const uint32_t valid = nvalid >= PVPT ? 0xffffu : ((1u << max(nvalid, 0)) - 1u);
+    if (greedy) {
+#pragma unroll
+      for (int j = 0; j < PVPT; ++j) {
+        if ((valid >> j) & 1u) {
+          const uint32_t h = rc.nd.temp ? (uint32_t)f2bf(final_value(bf2f((uint16_t)half16(x, j)), rc)) : half16(x, j);
+          best = umax(best, greedy_key_bits(h, c + j, log2bn));
+        }
+      }
+      return;
+    }
+    wtk_adopt(w, &st.cut, lane);
+    uint32_t m = 0;
+    if (rc.fast && !exact) {
+      const uint32_t lo[4] = {x[0], x[1], x[2], x[3]}, hi[4] = {x[4], x[5], x[6], x[7]};
+      m = (ge_mask8(lo, w.vmin2) | (ge_mask8(hi, w.vmin2) << 8)) & valid;
+      if (__any_sync(kFull, m)) push16(x, m, c, false);
+    } else {
+      const float thr = w.thr;
+#pragma unroll
+      for (int j = 0; j < PVPT; ++j)
+        if (((valid >> j) & 1u) && final_value(bf2f((uint16_t)half16(x, j)), rc) >= thr) m |= 1u << j;
+      if (__any_sync(kFull, m)) push16(x, m, c, rc.nd.temp);
+    }
+    absorb_if_full();
+  };
+
+  // groups of this warp: g = warp, warp + NW, ...; columns [c0 + g * PGROUP, +PGROUP)
+  const int ngroups = (int)((c1 - c0 + PGROUP - 1) / PGROUP);
+  auto gcol = [&](int g) { return c0 + (int64_t)g * PGROUP + (int64_t)PVPT * lane; };
+  auto gvalid = [&](int g) { return (int)max((int64_t)0, min((int64_t)PVPT, c1 - gcol(g))); };
+  constexpr int DM = MODE == kTma ? kVec : MODE;
+  bool werr = false;
+  if (MODE == kTma && rc.fast && !greedy && nchunks > 0) {
+    // cut bootstrap from the first chunk's lane maxima (see lane_max_publish)
+    if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+    const unsigned char* sp = smem_ring + warp * (PGROUP * 2) + lane * 32;
+    const uint4 u0 = *reinterpret_cast<const uint4*>(sp), u1 = *reinterpret_cast<const uint4*>(sp + 16);
+    const uint32_t x[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+    const uint32_t base = (uint32_t)(0xffff - (int)(gcol(warp) - c0));
+    uint32_t lm = 0;
+#pragma unroll
+    for (int j = 0; j < PVPT; ++j) {
+      const uint32_t h = half16(x, j);
+      if ((h & 0x7fffu) <= 0x7f80u) lm = umax(lm, (enc16(h) << 16) | (base - (uint32_t)j));
+    }
+    lane_max_publish(lm, st.vlm, warp, lane, final_of);
+    __syncthreads();
+    const float t = lane_max_min(st.vlm, lane);
+    if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
+  }
+
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
+    const int64_t c = gcol(g);
+    const int nv = gvalid(g);
+    uint32_t x[8];
+    const bool staged = k < nchunks;
+    if (staged) {
+      if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+      const unsigned char* sp = smem_ring + stage * PSTAGE + warp * (PGROUP * 2) + lane * 32;
+      const uint4 u0 = *reinterpret_cast<const uint4*>(sp), u1 = *reinterpret_cast<const uint4*>(sp + 16);
+      x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
+      x[4] = u1.x; x[5] = u1.y; x[6] = u1.z; x[7] = u1.w;
+    } else {
+      load_x16<DM>(xrow, c, nv, x);
+    }
+    process16(x, c, nv, false);
+    if (staged) {
+      // this warp has consumed its slice of the stage; the last of the NW warps refills it
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&st.rel[stage], 1) == NW - 1) {
+          atomicExch(&st.rel[stage], 0);
+          if (k + PNST < nchunks) {
+            __threadfence_block();
+            fence_proxy_async();
+            issue_chunk(k + PNST, stage);
+          }
+        }
+      }
+      if (++stage == PNST) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+  }
+  if (werr) atomicOr(ws.error, 1u);
+  pdl_trigger();
+
+  uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
+  if (greedy) {
+    best = warp_max_u64(best);
+    if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
+    __syncthreads();
+    if (tid == 0) {
+      stcg64(lists + (int64_t)split * kMaxK, st.best);
+      __threadfence();
+    }
+  } else {
+    if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    uint32_t fin[4];
+    block_fold(st.lists, warp, lane, fin);
+    if (warp == 0) {
+      const uint32_t last = __shfl_sync(kFull, fin[3], 31);
+      if (lane == 0) st.flag = last != 0;
+    }
+    __syncthreads();
+    if (!st.flag) {
+      // fewer than 128 finite candidates in this split: redo it keeping -inf logits
+      if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
+      __syncthreads();
+      wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
+      tq = false;
+      for (int gg = warp; gg < ngroups; gg += NW) {
+        uint32_t x[8];
+        load_x16<DM>(xrow, gcol(gg), gvalid(gg), x);
+        process16(x, gcol(gg), gvalid(gg), true);
+      }
+      if (w.qn) wtk_absorb(w, q, lane);
+      block_fold(st.lists, warp, lane, fin);
+    }
+    if (warp == 0) {
+      uint64_t* out = lists + (int64_t)split * kMaxK;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint64_t key = to_global<uint32_t>(fin[j], c0);
+        stcg64(out + 4 * lane + j, key);
+        if (key && !(a.flags & SONIC_FLAG_PHILOX) && (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
+      }
+      __threadfence();
+    }
+  }
+
+  if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
+
+  if (greedy) {
+    if (warp != 0) return;
+    uint64_t b = 0;
+    for (int s = lane; s < splits; s += 32) b = umax(b, ldcg64(lists + (int64_t)s * kMaxK));
+    b = warp_max_u64(b);
+    int64_t token = greedy_col(b, log2bn);
+    if (token < 0 || token >= a.vocab_size) token = -1;
+    if (lane == 0) a.tokens[r * a.tokens_stride] = (int32_t)token;
+    return;
+  }
+  uint64_t k[4];
+  block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
+  if (warp != 0) return;
   select_row(a, r, slot, ind, st.mp, k, lane);
 }
 
@@ -1928,6 +2193,19 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   const Workspace ws = carve(a->workspace, a->rows, a->rows, p.splits);
   const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
   const bool ind = a->d2t != nullptr;
+  const SonicSamplingParams& P = a->params;
+  if (!cand && !ind && !P.grammar && !P.decode_counts && !P.context_counts && !P.bias) {
+    // no per-column processor anywhere in the call: logits-only streaming kernel
+    const int pm = xvec ? kTma : kScalar;
+    const dim3 pgrid(p.splits, a->rows);
+    const bool ppdl = (a->flags & SONIC_FLAG_PDL) != 0;
+    const int pl2 = ilog2(a->block_n);
+    const cudaError_t pe =
+        pm == kTma ? launch(plain_kernel<kTma>, pgrid, (size_t)RING_BYTES, (cudaStream_t)stream, ppdl, *a, p.splits,
+                            p.cols, pl2, ws)
+                   : launch(plain_kernel<kScalar>, pgrid, 0, (cudaStream_t)stream, ppdl, *a, p.splits, p.cols, pl2, ws);
+    return check_launch(pe, what);
+  }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
   if (mode == kVec && !ind && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
   dim3 grid(p.splits, a->rows);

@@ -465,3 +465,32 @@ def test_multistep_varlen_single_row_requests(dev):
     ver, ref, kw, kh = run_multistep(x, tokens, cu_seqlens=cu.to(dev), lookahead=gamma, block_n=4096,
                                      update_counts=True, return_logprobs=True, **kw)
     _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(batch)), cu[:-1].tolist())
+
+
+@pytest.mark.parametrize("vocab", [128256, 50001])
+def test_plain_rows_no_processors(dev, vocab):
+    """Calls without grammar, counts or bias take the logits-only kernel: greedy and stochastic
+    rows, temperature, top-k / top-p / min-p, top-Z logprobs; aligned rows stream through the
+    bulk-copy ring, an odd vocabulary through scalar loads."""
+    rows = 40
+    params = workloads.config2_params(rows, 61)
+    ind = []
+    for i in range(rows):
+        from sonic_sampler_b200.core.flags import Indicator
+
+        f = Indicator.from_params(temperature=params.temperature[i], top_k=1 if i % 5 == 0 else params.top_k[i],
+                                  top_p=params.top_p[i], min_p=params.min_p[i], top_k_logprobs=6)
+        ind.append(int(f))
+    kw = dict(
+        indicators=torch.tensor(ind, dtype=torch.int32).to(torch.uint16).to(dev),
+        temperature=torch.tensor(params.temperature, dtype=BF16, device=dev),
+        top_k=torch.tensor(params.top_k, dtype=I32, device=dev),
+        top_p=torch.tensor(params.top_p, dtype=BF16, device=dev),
+        min_p=torch.tensor(params.min_p, dtype=BF16, device=dev),
+        top_k_logprobs=torch.full((rows,), 6, dtype=I32, device=dev),
+        gumbel_noise=workloads.log_exponential((rows, vocab), dev, 62),
+        return_logprobs=True, max_top_logprobs=6, logprobs_dtype=F32, block_n=4096,
+    )
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=63)
+    sel, ref, kw, kh = run_singular(x, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
