@@ -607,7 +607,7 @@ __device__ __forceinline__ void wtk_push(WarpTopK<K>& w, K* q, const K (&key)[VP
 // holds final keys and ties between final values fall back to the lowest column.
 template <typename K>
 __device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane, int tq, int tfast, float t,
-                                           float rt) {
+                                           float rt, int kth) {
   __syncwarp();
   K l[4];
 #pragma unroll
@@ -630,14 +630,18 @@ __device__ __noinline__ float absorb_queue(K* list, const K* q, int qn, int lane
 #pragma unroll
   for (int j = 0; j < 4; ++j) list[4 * lane + j] = l[j];
   __syncwarp();
-  const K last = __shfl_sync(kFull, l[3], 31);
+  // the kth kept key (kth = 128 unless only the first kth candidates can ever be selected)
+  const int src = (kth - 1) >> 2, jj = (kth - 1) & 3;
+  const K c0 = __shfl_sync(kFull, l[0], src), c1 = __shfl_sync(kFull, l[1], src);
+  const K c2 = __shfl_sync(kFull, l[2], src), c3 = __shfl_sync(kFull, l[3], src);
+  const K last = jj == 0 ? c0 : (jj == 1 ? c1 : (jj == 2 ? c2 : c3));
   return last != 0 ? key_value<K>(last) : __int_as_float(0xff800000);
 }
 
 template <typename K>
 __device__ __forceinline__ float wtk_absorb(WarpTopK<K>& w, const K* q, int lane, bool tq = false,
-                                            bool tfast = false, float t = 1.0f, float rt = 1.0f) {
-  const float r = absorb_queue<K>(w.list, q, w.qn, lane, tq, tfast, t, rt);
+                                            bool tfast = false, float t = 1.0f, float rt = 1.0f, int kth = kMaxK) {
+  const float r = absorb_queue<K>(w.list, q, w.qn, lane, tq, tfast, t, rt, kth);
   w.qn = 0;
   return r;
 }
@@ -770,6 +774,22 @@ __device__ __forceinline__ uint32_t vmin_pair(float thr, const RowConsts& rc) {
   return vmin_pair(thr, rc.nd.temp, rc.temp_fast, rc.temp, rc.rtemp);
 }
 
+// How many leading candidates of a row can ever matter: with top-k (k < 128) set, positions
+// >= k are masked to -inf before top-p, min-p, the softmax and the selection, so only the
+// exact top-k is needed (and the cut may come from the k-th key), unless top-Z logprobs
+// beyond k or the candidates' probabilities are written. Multistep rows keep 128 (their
+// stage-2 buffers hold all 128 candidates).
+__device__ __forceinline__ int needed_candidates(const SonicSingularArgs& a, uint32_t ind, int64_t slot, bool ms) {
+  const SonicSamplingParams& P = a.params;
+  if (ms || !(ind & 0x80) || !P.top_k || (a.flags & SONIC_FLAG_PROBABILITIES)) return kMaxK;
+  const int32_t k = P.top_k[slot];
+  if (k < 1 || k >= kMaxK) return kMaxK;
+  int z = 0;
+  if ((a.flags & SONIC_FLAG_LOGPROBS) && (ind & 0x400) && a.max_top_logprobs > 0 && P.top_logprobs)
+    z = min(P.top_logprobs[slot], a.max_top_logprobs);
+  return max(k, min(z, kMaxK));
+}
+
 // Shared-memory state of a single-row CTA; QC is the queue capacity of a warp (at least 127
 // plus the most keys a warp group can push).
 template <typename K, int QC = QCAP>
@@ -777,8 +797,8 @@ struct RowSmem {
   K queue[NW][QC];
   K lists[NW][kMaxK];
   unsigned long long cut;  // packed CTA cut, see pack_cut
-  float v16[NW];           // each warp's 16th kept key value (-inf while it keeps fewer)
-  float vlm[NW];           // each warp's 16th largest lane maximum (see lane_max_publish)
+  float v16[NW];           // each warp's m-th kept key value (-inf while it keeps fewer)
+  float vlm[NW];           // each warp's m-th largest lane maximum (see lane_max_publish)
   MaskParams mp;           // the slot's masking parameters (selection epilogue)
   int flag;
   unsigned long long best;
@@ -787,18 +807,20 @@ struct RowSmem {
   int rel[MAX_RING_STAGES];        // warps done with the stage
 };
 
-// After an absorb: the warp's new threshold candidates are its own 128th key value and the
-// smallest 16th key value over all warps (the 8 top-16 sets are 128 distinct keys).
+// After an absorb: the warp's new threshold candidates are its own kk-th key value (own) and
+// the smallest m-th key value over all warps (the 8 top-m sets are 8m >= kk distinct keys),
+// kk the number of leading candidates the row needs exactly (128 unless top-k is smaller).
 template <typename K>
-__device__ __forceinline__ float absorbed_cut(const WarpTopK<K>& w, float own128, float* v16, int warp, int lane) {
-  const K k16 = w.list[15];
-  if (lane == 0) reinterpret_cast<volatile float*>(v16)[warp] = k16 ? key_value<K>(k16) : __int_as_float(0xff800000);
+__device__ __forceinline__ float absorbed_cut(const WarpTopK<K>& w, float own, float* v16, int warp, int lane,
+                                             int m = 16) {
+  const K km = w.list[m - 1];
+  if (lane == 0) reinterpret_cast<volatile float*>(v16)[warp] = km ? key_value<K>(km) : __int_as_float(0xff800000);
   __syncwarp();
-  float m = lane < NW ? reinterpret_cast<volatile float*>(v16)[lane] : __int_as_float(0x7f800000);
+  float lo = lane < NW ? reinterpret_cast<volatile float*>(v16)[lane] : __int_as_float(0x7f800000);
 #pragma unroll
-  for (int d = 4; d >= 1; d >>= 1) m = fminf(m, __shfl_xor_sync(kFull, m, d));
-  m = __shfl_sync(kFull, m, 0);
-  return fmaxf(own128, m);
+  for (int d = 4; d >= 1; d >>= 1) lo = fminf(lo, __shfl_xor_sync(kFull, lo, d));
+  lo = __shfl_sync(kFull, lo, 0);
+  return fmaxf(own, lo);
 }
 
 // descending bitonic sort of one value per lane
@@ -815,13 +837,15 @@ __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v, int lane) {
   return v;
 }
 
-// Each lane's largest key belongs to a distinct column, so the 16th largest lane maximum of
-// every warp bounds 8 x 16 = 128 distinct keys of the split from below: the smallest of
-// those over the warps is a valid cut. lane_max_publish stores a warp's 16th largest lane
-// maximum (as a final value); lane_max_min reads the smallest over the warps.
+// Each lane's largest key belongs to a distinct column, so the m-th largest lane maximum of
+// every warp bounds 8m distinct keys of the split from below: with 8m >= kk (the leading
+// candidates the row needs; m = 16 for all 128) the smallest of those over the warps is a
+// valid cut. lane_max_publish stores a warp's m-th largest lane maximum (as a final value);
+// lane_max_min reads the smallest over the warps.
 template <typename F>
-__device__ __forceinline__ void lane_max_publish(uint32_t lmax, float* vlm, int warp, int lane, F final_of) {
-  const uint32_t k16 = __shfl_sync(kFull, warp_sort32_desc(lmax, lane), 15);
+__device__ __forceinline__ void lane_max_publish(uint32_t lmax, float* vlm, int warp, int lane, F final_of,
+                                                 int m = 16) {
+  const uint32_t k16 = __shfl_sync(kFull, warp_sort32_desc(lmax, lane), m - 1);
   if (lane == 0)
     reinterpret_cast<volatile float*>(vlm)[warp] = k16 ? final_of(key_value<uint32_t>(k16)) : __int_as_float(0xff800000);
 }
@@ -1007,6 +1031,8 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const RowConsts rc = row_consts(P, slot, ind);
   // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
   const bool greedy = (ind & 0x40) != 0 && !cand_out;
+  const int kk = needed_candidates(a, ind, slot, MS);  // exact leading candidates needed
+  const int mm = (kk + NW - 1) / NW;                   // of them per warp (cut rules)
   // drafted tokens counted as decoded: singular counts all `lookahead` drafted tokens of the
   // slot (ops/prologue.py:175-184); multistep step s counts the request's first s
   const int ntok = !rc.nd.dec ? 0 : (MS ? step : (a.drafted_tokens ? a.lookahead : 0));
@@ -1063,7 +1089,8 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
-      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp), st.v16, warp, lane);
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
+                                   lane, mm);
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
     }
   };
@@ -1221,7 +1248,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       const uint32_t h = half_of(y, j);
       if (((ok >> j) & 1u) && (h & 0x7fffu) <= 0x7f80u) lm = umax(lm, (enc16(h) << 16) | (base - (uint32_t)j));
     }
-    lane_max_publish(lm, st.vlm, warp, lane, final_of);
+    lane_max_publish(lm, st.vlm, warp, lane, final_of, mm);
     __syncthreads();
     const float t = lane_max_min(st.vlm, lane);
     if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
@@ -1303,12 +1330,15 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
     if (warp == 0) {
-      const uint32_t last = __shfl_sync(kFull, fin[3], 31);
+      // the split holds at least kk finite candidates when list position kk - 1 is taken
+      const int jj = (kk - 1) & 3;
+      const uint32_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
+      const uint32_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
       if (lane == 0) st.flag = last != 0;
     }
     __syncthreads();
     if (!st.flag) {
-      // fewer than 128 finite candidates in this split: redo it keeping -inf logits,
+      // fewer than kk finite candidates in this split: redo it keeping -inf logits,
       // through the exact path
       if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
       __syncthreads();
@@ -1437,6 +1467,8 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
   const uint32_t ind = P.indicators[slot];
   const RowConsts rc = row_consts(P, slot, ind);
   const bool greedy = (ind & 0x40) != 0;
+  const int kk = needed_candidates(a, ind, slot, false);  // exact leading candidates needed
+  const int mm = (kk + NW - 1) / NW;                      // of them per warp (cut rules)
   const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
   const int nchunks = MODE == kTma ? (int)((c1 - c0) / PCH) : 0;
   auto issue_chunk = [&](int i, int stage) {  // one thread
@@ -1468,7 +1500,8 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
-      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp), st.v16, warp, lane);
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
+                                   lane, mm);
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
     }
   };
@@ -1534,7 +1567,7 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
       const uint32_t h = half16(x, j);
       if ((h & 0x7fffu) <= 0x7f80u) lm = umax(lm, (enc16(h) << 16) | (base - (uint32_t)j));
     }
-    lane_max_publish(lm, st.vlm, warp, lane, final_of);
+    lane_max_publish(lm, st.vlm, warp, lane, final_of, mm);
     __syncthreads();
     const float t = lane_max_min(st.vlm, lane);
     if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
@@ -1594,12 +1627,15 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
     if (warp == 0) {
-      const uint32_t last = __shfl_sync(kFull, fin[3], 31);
+      // the split holds at least kk finite candidates when list position kk - 1 is taken
+      const int jj = (kk - 1) & 3;
+      const uint32_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
+      const uint32_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
       if (lane == 0) st.flag = last != 0;
     }
     __syncthreads();
     if (!st.flag) {
-      // fewer than 128 finite candidates in this split: redo it keeping -inf logits
+      // fewer than kk finite candidates in this split: redo it keeping -inf logits
       if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
       __syncthreads();
       wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
@@ -1730,6 +1766,8 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
   K* q = st.queue[warp];
   WarpTopK<K> w;
   wtk_init(w, st.lists[warp], kFiniteFloor, lane);
+  const int kk = min(max(a.k, 1), kMaxK);  // only the first k keys of each split are exact
+  const int mm = (kk + NW - 1) / NW;
 
   auto consume = [&](const float (&x)[VPT], int64_t c, int nvalid) {
     wtk_adopt(w, &st.cut, lane);
@@ -1751,7 +1789,7 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
       wtk_push(w, q, key, m, lane);
     }
     if (w.qn >= kMaxK) {
-      const float t = absorbed_cut(w, wtk_absorb(w, q, lane), st.v16, warp, lane);
+      const float t = absorbed_cut(w, wtk_absorb(w, q, lane, false, false, 1.0f, 1.0f, kk), st.v16, warp, lane, mm);
       if (t > w.thr) wtk_raise(w, &st.cut, t, 0u, lane);
     }
   };
@@ -1784,12 +1822,15 @@ __global__ void __launch_bounds__(NT) topk_kernel(const SonicTopKArgs a, int spl
   K fin[4];
   block_fold(st.lists, warp, lane, fin);
   if (warp == 0) {
-    const K last = __shfl_sync(kFull, fin[3], 31);
+    // the split holds at least kk finite values when list position kk - 1 is taken
+    const int jj = (kk - 1) & 3;
+    const K f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
+    const K last = __shfl_sync(kFull, f, (kk - 1) >> 2);
     if (lane == 0) st.flag = last != 0;
   }
   __syncthreads();
   if (!st.flag) {
-    // fewer than 128 finite values in this split: redo it keeping -inf
+    // fewer than kk finite values in this split: redo it keeping -inf
     if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
     __syncthreads();
     wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);

@@ -494,3 +494,88 @@ def test_plain_rows_no_processors(dev, vocab):
     x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=63)
     sel, ref, kw, kh = run_singular(x, **kw)
     assert_selection_equal(sel, ref, kw, kh)
+
+
+# ----------------------------------------------------------------------------------------
+# rows that need fewer than 128 exact candidates (top-k below 128)
+# ----------------------------------------------------------------------------------------
+
+_KS = [2, 3, 7, 8, 9, 15, 16, 17, 31, 33, 63, 64, 65, 100, 127, 128]
+_ZS = [0, 1, 5, 20]
+
+
+def _small_k_case(dev, rows, vocab, seed, density):
+    """Buffers whose rows cycle through top-k values around the per-warp cut boundaries (k = 8m,
+    8m +- 1) and top-Z requests below and above k; logits on a coarse grid so that many values
+    tie at the k-th place."""
+    b = _params(dev, rows, vocab, seed=seed, grammar_density=density, top_logprobs=5)
+    top_k = torch.tensor([_KS[i % len(_KS)] for i in range(rows)], dtype=I32)
+    z = torch.tensor([_ZS[(i // len(_KS)) % len(_ZS)] for i in range(rows)], dtype=I32)
+    ind = b.flags.target.cpu().to(torch.int32) & ~(0x40 | 0x80 | 0x400)
+    ind |= torch.where((top_k > 1) & (top_k < 128), 0x80, 0).to(torch.int32)
+    ind |= torch.where(z > 0, 0x400, 0).to(torch.int32)
+    b.top_k.copy_(top_k.to(dev))
+    b.top_logprobs.copy_(z.to(dev))
+    b.flags.packed[:, 0] = ind.to(torch.uint16).to(dev)
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=seed)
+    x = (x.float() * 2).round().div(2).to(BF16)
+    return x, b
+
+
+def _assert_top_z_equal(sel, ref, kh, cap):
+    """The first min(Z, cap) top logprobs and tokens of every row that asks for them (entries
+    past Z are not written)."""
+    z = kh["top_k_logprobs"].clamp(max=cap)
+    want = (kh["indicators"].to(torch.int32) & 0x400) != 0
+    a_lp, b_lp = bits(sel.logprobs.top_k.logprobs), bits(ref.logprobs.top_k.logprobs)
+    a_tk, b_tk = sel.logprobs.top_k.tokens.cpu(), ref.logprobs.top_k.tokens
+    for i in range(a_lp.size(0)):
+        n = int(z[i]) if bool(want[i]) else 0
+        assert torch.equal(a_lp[i, :n], b_lp[i, :n]), i
+        assert torch.equal(a_tk[i, :n], b_tk[i, :n]), i
+
+
+@pytest.mark.parametrize("density", [0.3, 0.002])
+def test_small_top_k_rows(dev, density):
+    """Rows with top-k < 128 keep only their first k candidates exact (the streaming cut comes
+    from the k-th key). A sparse grammar leaves some splits with fewer than k allowed columns,
+    which takes the -inf redo. Tokens, logprobs, top-Z (also Z > k) and counts must match."""
+    x, b = _small_k_case(dev, 64, 128256, seed=71, density=density)
+    sel, ref, kw, kh = run_singular(x, update_counts=True, return_logprobs=True, max_top_logprobs=20,
+                                    logprobs_dtype=F32, **buffer_kwargs(b))
+    assert_selection_equal(sel, ref, kw, kh)
+    _assert_top_z_equal(sel, ref, kh, 20)
+
+
+def test_small_top_k_rows_logits_only(dev):
+    """The same rows through the logits-only kernel (no grammar, counts or bias)."""
+    x, b = _small_k_case(dev, 64, 128256, seed=72, density=0.3)
+    kw = buffer_kwargs(b)
+    for key in ("grammar", "context_counts", "decode_counts", "logit_bias"):
+        kw.pop(key)
+    ind = kw["indicators"].cpu().to(torch.int32) & ~0x1f  # no grammar / penalty / bias bits
+    kw["indicators"] = ind.to(torch.uint16).to(dev)
+    sel, ref, kw, kh = run_singular(x, return_logprobs=True, max_top_logprobs=20, logprobs_dtype=F32, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
+    _assert_top_z_equal(sel, ref, kh, 20)
+
+
+@pytest.mark.parametrize("k", [1, 2, 8, 16, 64, 128])
+def test_topk_small_k_with_ties(dev, k):
+    from oracle import oracle
+    from sonic_sampler_b200 import ops
+    from sonic_sampler_b200.interface import UnshardedBoundedTopK
+
+    rows, vocab = 8, 128256
+    x = workloads.peaked_logits(rows, vocab, sigma=2.0, peaks=8, lift=10.0, device=dev, seed=k, dtype=F32)
+    x = x.mul(2).round().div(2)
+    topk = UnshardedBoundedTopK.initialize(vocab, batch_size=rows, k=k).clear()
+    values, indices = topk(x)
+    torch.cuda.synchronize()
+    vals = values.reshape(-1)[: rows * k].view(rows, k).cpu()
+    idx = indices.reshape(-1)[: rows * k].view(rows, k).cpu()
+    hv = torch.empty(rows * k, dtype=F32)
+    hi = torch.empty(rows * k, dtype=I32)
+    oracle.bounded_topk(ops.topk_args(x.cpu(), vocab_size=vocab, k=k, block_n=topk.block_n, values=hv, indices=hi))
+    assert torch.equal(idx, hi.view(rows, k))
+    assert torch.equal(bits(vals), bits(hv.view(rows, k)))
