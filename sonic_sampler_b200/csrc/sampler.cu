@@ -823,6 +823,13 @@ __device__ __forceinline__ float absorbed_cut(const WarpTopK<K>& w, float own, f
   return fmaxf(own, lo);
 }
 
+// elementwise max of two bf16 pairs; a NaN loses to the other operand (IEEE maxNum)
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // descending bitonic sort of one value per lane
 __device__ __forceinline__ uint32_t warp_sort32_desc(uint32_t v, int lane) {
 #pragma unroll
@@ -1413,14 +1420,15 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 // plain singular rows: no grammar, counts, bias, d2t or drafted tokens anywhere in the call
 // (logits, optional temperature, then the usual masking and selection). Same machinery as
 // singular_kernel with wider groups: 16 columns a lane, 512 a warp, 4096-column chunks of
-// logits only (8 KB a stage, 9 stages in the ring).
+// logits only (8 KB a stage; 5 stages and 3 CTAs an SM for grids of several waves, else 9).
 // ---------------------------------------------------------------------------------------
 
 constexpr int PVPT = 16;               // columns per lane
 constexpr int PGROUP = PVPT * 32;      // columns per warp group
 constexpr int PCH = PGROUP * NW;       // columns per chunk
 constexpr int PSTAGE = PCH * 2;        // bytes per stage
-constexpr int PNST = RING_BYTES / PSTAGE < MAX_RING_STAGES ? RING_BYTES / PSTAGE : MAX_RING_STAGES;
+constexpr int PNST_WAVES = 5;         // ring stages of a multi-wave grid: 40 KB, 3 CTAs an SM
+constexpr int PNST_ONE = 9;           // of a one-wave grid: 72 KB, more bytes in flight a CTA
 constexpr int PQCAP = kMaxK + PGROUP;  // a warp appends at most 512 keys per group
 
 // 16 logits of one lane, pre-temperature bf16 pairs; `nvalid` columns valid (-inf beyond)
@@ -1446,8 +1454,8 @@ __device__ __forceinline__ uint32_t half16(const uint32_t (&x)[8], int j) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
-                                                   Workspace ws) {
+__global__ void __launch_bounds__(NT, 3) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
+                                                      Workspace ws, int nst) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1481,12 +1489,12 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
     if (MODE == kTma) {
-      for (int i = 0; i < PNST; ++i) {
+      for (int i = 0; i < nst; ++i) {
         mbar_init(&st.bars[i], 1);
         st.rel[i] = 0;
       }
       mbar_fence_init();
-      for (int i = 0; i < min(nchunks, PNST); ++i) issue_chunk(i, i);
+      for (int i = 0; i < min(nchunks, nst); ++i) issue_chunk(i, i);
     }
   }
   __syncthreads();
@@ -1573,6 +1581,13 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
     if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
   }
 
+  // Cut refresh: each lane keeps the running maximum of the logits it has streamed through
+  // the ring (bf16 pairs). As for the bootstrap, the m-th largest lane maximum of every warp
+  // bounds 8m distinct columns, so the smallest over the warps is a valid cut; a stale value
+  // of another warp is smaller, so also valid. Refreshed after the warp's groups 1, 3 and 7:
+  // early, when the cut is still low and most groups push.
+  const bool refresh = MODE == kTma && rc.fast && !greedy && nchunks > 0;
+  uint32_t lmv = 0xff80ff80u;
   int stage = 0;
   uint32_t phase = 0;
   for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
@@ -1590,6 +1605,19 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
       load_x16<DM>(xrow, c, nv, x);
     }
     process16(x, c, nv, false);
+    if (refresh && staged) {
+      const uint32_t m01 = bf2_max(bf2_max(x[0], x[1]), bf2_max(x[2], x[3]));
+      const uint32_t m23 = bf2_max(bf2_max(x[4], x[5]), bf2_max(x[6], x[7]));
+      lmv = bf2_max(lmv, bf2_max(m01, m23));
+      if (k == 1 || k == 3 || k == 7) {
+        const uint32_t lo = lmv & 0xffffu, hi = lmv >> 16;
+        const uint32_t h = enc16(lo) >= enc16(hi) ? lo : hi;
+        lane_max_publish((h & 0x7fffu) <= 0x7f80u ? enc16(h) << 16 : 0u, st.vlm, warp, lane, final_of, mm);
+        __syncwarp();
+        const float t = lane_max_min(st.vlm, lane);
+        if (t > w.thr) wtk_raise(w, &st.cut, t, vmin_pair(t, rc), lane);
+      }
+    }
     if (staged) {
       // this warp has consumed its slice of the stage; the last of the NW warps refills it
       __syncwarp();
@@ -1597,14 +1625,14 @@ __global__ void __launch_bounds__(NT) plain_kernel(const SonicSingularArgs a, in
         __threadfence_block();
         if (atomicAdd(&st.rel[stage], 1) == NW - 1) {
           atomicExch(&st.rel[stage], 0);
-          if (k + PNST < nchunks) {
+          if (k + nst < nchunks) {
             __threadfence_block();
             fence_proxy_async();
-            issue_chunk(k + PNST, stage);
+            issue_chunk(k + nst, stage);
           }
         }
       }
-      if (++stage == PNST) {
+      if (++stage == nst) {
         stage = 0;
         phase ^= 1u;
       }
@@ -2241,10 +2269,13 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     const dim3 pgrid(p.splits, a->rows);
     const bool ppdl = (a->flags & SONIC_FLAG_PDL) != 0;
     const int pl2 = ilog2(a->block_n);
+    // a grid of several waves keeps 3 CTAs an SM busy (their fixed costs overlap); one wave
+    // streams longer rows per CTA and takes a deeper ring instead
+    const int nst = (int64_t)p.splits * a->rows > TARGET_CTAS ? PNST_WAVES : PNST_ONE;
     const cudaError_t pe =
-        pm == kTma ? launch(plain_kernel<kTma>, pgrid, (size_t)RING_BYTES, (cudaStream_t)stream, ppdl, *a, p.splits,
-                            p.cols, pl2, ws)
-                   : launch(plain_kernel<kScalar>, pgrid, 0, (cudaStream_t)stream, ppdl, *a, p.splits, p.cols, pl2, ws);
+        pm == kTma ? launch(plain_kernel<kTma>, pgrid, (size_t)nst * PSTAGE, (cudaStream_t)stream, ppdl, *a, p.splits,
+                            p.cols, pl2, ws, nst)
+                   : launch(plain_kernel<kScalar>, pgrid, 0, (cudaStream_t)stream, ppdl, *a, p.splits, p.cols, pl2, ws, 0);
     return check_launch(pe, what);
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;

@@ -204,3 +204,55 @@ def config5(device, seed: int = 0, batch: int = 1024, vocab: int = 256000):
         top_p=torch.full((batch,), 0.95, dtype=BF16, device=dev),
         philox_seed=1234,
     )
+
+
+def runner(name: str, device):
+    """A no-argument callable that runs benchmark config `name` once through the public
+    interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep;
+    5: fused_singular with Philox noise; 1: UnshardedBoundedTopK)."""
+    dev = torch.device(device)
+    if name == "config1":
+        from sonic_sampler_b200.interface import UnshardedBoundedTopK
+
+        c = config1(dev)
+        topk = UnshardedBoundedTopK.initialize(32000, batch_size=8, k=c["k"])
+        return lambda: topk(c["logits"])
+    if name == "config2":
+        from sonic_sampler_b200.interface import UnshardedFusedSingular
+
+        c = config2(dev, seed=1000)
+        sampler = UnshardedFusedSingular.initialize(128256, batch_size=64)
+        return lambda: sampler.autoregressive(c["logits"], c["buffers"], logprobs=True)
+    if name == "config3":
+        from sonic_sampler_b200.interface.functional.multistep import fused_multistep
+
+        c = config3(dev, seed=8)
+        b = c["buffers"]
+        kw = dict(grammar=b.grammar, context_counts=b.repetition.counts.context,
+                  decode_counts=b.repetition.counts.decode, repetition_penalties=b.repetition.multiplicative,
+                  frequency_penalties=b.repetition.frequency, presence_penalties=b.repetition.presence,
+                  logit_bias=b.bias, temperature=b.temperature, top_k=b.top_k, top_p=b.top_p, min_p=b.min_p,
+                  top_k_logprobs=b.top_logprobs, gumbel_noise=b.weights.gumbel.target, uniform_noise=b.weights.uniform)
+        return lambda: fused_multistep(c["flat_logits"], b.flags.target, c["flat_tokens"], cu_seqlens=c["cu_seqlens"],
+                                       lookahead=c["gamma"], max_top_logprobs=20, return_logprobs=True,
+                                       draft_probabilities=c["probabilities"], block_n=4096, **kw)
+    if name == "config5":
+        from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+        c = config5(dev, seed=1)
+        kw = dict(indicators=c["indicators"], top_k=c["top_k"], top_p=c["top_p"], block_n=4096,
+                  philox_seed=c["philox_seed"], philox_offset=17, return_logprobs=True)
+        return lambda: fused_singular(c["logits"], **kw)
+    raise ValueError(f"unknown workload {name!r}")
+
+
+if __name__ == "__main__":
+    # python -m sonic_sampler_b200.workloads config5 [calls]: run a config `calls` times on
+    # cuda:0 (the target of the ncu commands that produced the profiles)
+    import sys
+
+    fn = runner(sys.argv[1], "cuda")
+    for _ in range(int(sys.argv[2]) if len(sys.argv) > 2 else 6):
+        fn()
+    torch.cuda.synchronize()
+    print("ok", sys.argv[1])
