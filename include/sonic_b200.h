@@ -254,6 +254,17 @@ sonic_status sonic_merge_candidates(const SonicSingularArgs* args, const uint64_
  * on the same device) race and must be serialised by the caller. */
 sonic_status sonic_fused_singular_static(const SonicSingularArgs* args, void* stream);
 
+/* Noise staging: for each i < count, row r = indices[i] (i32 or i64, index_dtype); unless
+ * indicator[r] has the greedy bit (0x40), copy `cols` elements of `elem_bytes` bytes from
+ * source + r * stride to target + r * stride (elements; the same row stride for both).
+ * Indices outside [0, rows) are skipped. Runs on `stream`, allocates nothing, never
+ * synchronises. Replaces ops/copy.py:21-127 (`indexed_copy`, `indexed_copy_kernel`), called
+ * by `GumbelNoise.stage_weights` (core/buffer.py:151-157) to move the draft noise of the
+ * stochastic slots into the target noise after verification. */
+sonic_status sonic_indexed_copy(const void* source, void* target, int64_t rows, int64_t stride, int64_t cols,
+                                int32_t elem_bytes, const void* indices, int32_t index_dtype, int32_t count,
+                                const uint16_t* indicator, void* stream);
+
 /* ABI version (SONIC_B200_ABI_VERSION) the library was built with. */
 int32_t sonic_abi_version(void);
 /* Message of the calling thread's last failed call ("" when none). */

@@ -79,3 +79,17 @@ def log(x: float) -> float:
 
 def philox_log_exponential(seed: int, offset: int, slot: int, token: int) -> float:
     return load().ox_philox_log_exponential(seed, offset, slot, token)
+
+
+def indexed_copy(source, target, indices, indicator) -> None:
+    """CPU restatement of the reference's noise staging (ops/copy.py:21-55
+    `indexed_copy_kernel`, launched by `indexed_copy` at :86-109): program (i, block) reads row
+    j = indices[i] and, unless indicator[j] has the greedy bit 0x40, copies that row's
+    flattened columns of `source` into the same offsets of `target`. Host tensors; `target`
+    is updated in place."""
+    src = source.reshape(source.size(0), -1)
+    dst = target.view(target.size(0), -1)
+    for i in range(indices.numel()):
+        j = int(indices[i])
+        if not (int(indicator[j]) & 0x40):
+            dst[j].copy_(src[j])

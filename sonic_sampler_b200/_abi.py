@@ -175,6 +175,7 @@ EXPORTED_SYMBOLS = (
     "sonic_fused_singular_static",
     "sonic_shard_candidates",
     "sonic_merge_candidates",
+    "sonic_indexed_copy",
     "sonic_abi_version",
     "sonic_last_error",
 )
@@ -205,6 +206,9 @@ def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.sonic_shard_candidates.restype = _i32
     lib.sonic_merge_candidates.argtypes = [ctypes.POINTER(SingularArgs), _vp, _i32, _vp]
     lib.sonic_merge_candidates.restype = _i32
+    lib.sonic_indexed_copy.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i32, _vp, _i32, _i32,
+                                       _vp, _vp]
+    lib.sonic_indexed_copy.restype = _i32
     lib.sonic_abi_version.argtypes = []
     lib.sonic_abi_version.restype = _i32
     lib.sonic_last_error.argtypes = []

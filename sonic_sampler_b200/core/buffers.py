@@ -81,6 +81,17 @@ class GumbelNoise:
     target: Tensor
     draft: Tensor
 
+    def stage_weights(self, indices: Tensor, indicator: Tensor, stream: torch.cuda.Stream | None = None) -> "GumbelNoise":
+        """Copy the draft noise of the slots at `indices` whose indicator is not greedy into the
+        target noise (reference `core/buffer.py:151-157`), on `stream` when given."""
+        from contextlib import nullcontext
+
+        from sonic_sampler_b200.ops import indexed_copy
+
+        with (torch.cuda.stream(stream) if stream is not None else nullcontext()):
+            indexed_copy(self.draft, self.target, indices, indicator)
+        return self
+
 
 @dataclass
 class StochasticWeights:

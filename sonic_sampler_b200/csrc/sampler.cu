@@ -2431,6 +2431,171 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
 }  // extern "C"
 
 // ---------------------------------------------------------------------------------------
+// noise staging (ops/copy.py:21-127 indexed_copy): the rows of `source` named by `indices`
+// whose indicator lacks the greedy bit are copied to the same rows of `target`
+//
+// A pure HBM stream (read + write once). Each CTA is one issuing thread driving a ring of
+// 16 KB 1-D bulk copies: global -> shared on an mbarrier, then shared -> global as a bulk
+// store; a stage is refilled once its store has read it (wait_group.read). The CTA's chunks
+// are a contiguous run of the selected rows' 16 KB chunks. Rows whose bytes, base addresses
+// or stride are not 16-byte multiples take an element-wise kernel instead.
+// ---------------------------------------------------------------------------------------
+
+namespace sonic {
+
+constexpr int CP_CHUNK = 16384;  // bytes of one bulk copy
+constexpr int CP_STAGES = 4;     // 64 KB of ring: 3 CTAs an SM
+constexpr int CP_CTAS_PER_SM = 3;
+
+struct CopyArgs {
+  const unsigned char* src;
+  unsigned char* dst;
+  int64_t stride;  // bytes between rows (source and target alike)
+  int64_t row;     // bytes copied per row
+  const void* indices;
+  int32_t index_dtype;
+  int32_t count;
+  const uint16_t* indicator;
+  int64_t rows;  // rows of source / target: other indices are skipped
+};
+
+__device__ __forceinline__ void bulk_store(void* gdst, const void* ssrc, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(smem_addr(ssrc)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// every committed bulk store has finished reading its shared memory
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// every committed bulk store has completed
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__global__ void __launch_bounds__(32) indexed_copy_kernel(const CopyArgs c, int64_t chunks_per_row, int64_t total) {
+  extern __shared__ __align__(128) unsigned char ring[];
+  __shared__ uint64_t bars[CP_STAGES];
+  if (threadIdx.x != 0) return;
+  const int64_t G = gridDim.x;
+  const int64_t q0 = (int64_t)blockIdx.x * total / G;
+  const int64_t n = ((int64_t)blockIdx.x + 1) * total / G - q0;
+  for (int i = 0; i < CP_STAGES; ++i) mbar_init(&bars[i], 1);
+  mbar_fence_init();
+  unsigned char* dst[CP_STAGES];
+  uint32_t bytes[CP_STAGES];
+  uint32_t live = 0;  // stages holding a chunk to store
+  // chunk j of this CTA into stage j % CP_STAGES: a bulk load, or a plain arrival for a
+  // chunk of a greedy row (nothing to copy), so that every stage completes once per use
+  auto issue = [&](int64_t j) {
+    const int s = (int)(j % CP_STAGES);
+    const int64_t q = q0 + j;
+    const int64_t i = q / chunks_per_row, piece = q % chunks_per_row;
+    const int64_t r = load_index(c.indices, c.index_dtype, i);
+    if (r < 0 || r >= c.rows || (c.indicator[r] & 0x40)) {
+      live &= ~(1u << s);
+      mbar_arrive(&bars[s]);
+      return;
+    }
+    const int64_t off = r * c.stride + piece * CP_CHUNK;
+    const uint32_t nb = (uint32_t)min((int64_t)CP_CHUNK, c.row - piece * CP_CHUNK);
+    live |= 1u << s;
+    dst[s] = c.dst + off;
+    bytes[s] = nb;
+    mbar_expect_tx(&bars[s], nb);
+    bulk_load(ring + s * CP_CHUNK, c.src + off, nb, &bars[s]);
+  };
+  for (int64_t j = 0; j < min(n, (int64_t)CP_STAGES); ++j) issue(j);
+  for (int64_t j = 0; j < n; ++j) {
+    const int s = (int)(j % CP_STAGES);
+    mbar_wait_bounded(&bars[s], (uint32_t)((j / CP_STAGES) & 1), WAIT_LIMIT);
+    if ((live >> s) & 1u) {
+      bulk_store(dst[s], ring + s * CP_CHUNK, bytes[s]);
+      bulk_commit();
+    }
+    if (j + CP_STAGES < n) {
+      bulk_wait_read_all();  // the store just issued from stage s has read it
+      issue(j + CP_STAGES);
+    }
+  }
+  bulk_wait_all();
+}
+
+// the same copy element by element (rows not in 16-byte units)
+template <typename E>
+__global__ void __launch_bounds__(256) indexed_copy_elems(const CopyArgs c, int64_t elems) {
+  for (int64_t i = blockIdx.y; i < c.count; i += gridDim.y) {
+    const int64_t r = load_index(c.indices, c.index_dtype, i);
+    if (r < 0 || r >= c.rows || (c.indicator[r] & 0x40)) continue;
+    const E* src = reinterpret_cast<const E*>(c.src + r * c.stride);
+    E* dst = reinterpret_cast<E*>(c.dst + r * c.stride);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < elems; e += (int64_t)gridDim.x * blockDim.x)
+      __stcs(dst + e, __ldcs(src + e));
+  }
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return n > 0 ? n : 148;
+}
+
+}  // namespace sonic
+
+extern "C" {
+
+sonic_status sonic_indexed_copy(const void* source, void* target, int64_t rows, int64_t stride, int64_t cols,
+                                int32_t elem_bytes, const void* indices, int32_t index_dtype, int32_t count,
+                                const uint16_t* indicator, void* stream) {
+  if (count < 0 || cols < 0 || stride < 0 || rows < 0)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "rows, count, cols and stride must be >= 0");
+  if (count == 0 || cols == 0 || rows == 0) return SONIC_OK;
+  if (!source || !target || !indices || !indicator)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "source, target, indices and indicator must not be NULL");
+  if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4 && elem_bytes != 8)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "elem_bytes must be 1, 2, 4 or 8");
+  if (index_dtype != SONIC_DTYPE_I32 && index_dtype != SONIC_DTYPE_I64)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "indices dtype must be i32 or i64");
+  if (cols > stride) return fail(SONIC_ERR_INVALID_ARGUMENT, "cols must not exceed the row stride");
+  CopyArgs c;
+  c.src = (const unsigned char*)source;
+  c.dst = (unsigned char*)target;
+  c.stride = stride * elem_bytes;
+  c.row = cols * elem_bytes;
+  c.indices = indices;
+  c.index_dtype = index_dtype;
+  c.count = count;
+  c.indicator = indicator;
+  c.rows = rows;
+  cudaStream_t st = (cudaStream_t)stream;
+  cudaError_t e;
+  if (aligned(source, 16) && aligned(target, 16) && c.stride % 16 == 0 && c.row % 16 == 0) {
+    const int64_t cpr = (c.row + CP_CHUNK - 1) / CP_CHUNK;
+    const int64_t total = cpr * count;
+    const int64_t grid = std::min<int64_t>(total, (int64_t)sm_count() * CP_CTAS_PER_SM);
+    const size_t smem = (size_t)CP_STAGES * CP_CHUNK;
+    e = cudaFuncSetAttribute(indexed_copy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e == cudaSuccess) {
+      indexed_copy_kernel<<<dim3((unsigned)grid), dim3(32), smem, st>>>(c, cpr, total);
+      e = cudaGetLastError();
+    }
+  } else {
+    const dim3 grid((unsigned)std::min<int64_t>((cols + 255) / 256, 64), (unsigned)std::min<int64_t>(count, 65535));
+    switch (elem_bytes) {
+      case 1: indexed_copy_elems<uint8_t><<<grid, 256, 0, st>>>(c, cols); break;
+      case 2: indexed_copy_elems<uint16_t><<<grid, 256, 0, st>>>(c, cols); break;
+      case 4: indexed_copy_elems<uint32_t><<<grid, 256, 0, st>>>(c, cols); break;
+      default: indexed_copy_elems<unsigned long long><<<grid, 256, 0, st>>>(c, cols); break;
+    }
+    e = cudaGetLastError();
+  }
+  return check_launch(e, "sonic_indexed_copy");
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------------------
 // singular call without a caller workspace
 //
 // For hosts that cannot allocate device memory for this library: a serving engine that has

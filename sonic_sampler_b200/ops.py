@@ -387,3 +387,31 @@ def launch_topk(args: TopKArgs, device: torch.device) -> None:
     lib = _abi.load_library()
     with torch.cuda.device(device):
         _abi.check(lib.sonic_bounded_topk(ctypes.byref(args), ctypes.c_void_p(_stream(device))), lib)
+
+
+def indexed_copy(source: Tensor, target: Tensor, indices: Tensor, indicator: Tensor) -> None:
+    """Fused `index_select` of `source` rows at `indices` and `index_copy_` into `target`, only
+    for rows whose `indicator` lacks the greedy bit 0x40 (reference `ops/copy.py:86-109`).
+
+    `source` and `target` have the same shape, dtype and row stride, with each row contiguous
+    (the reference copies `source.flatten(1).size(1)` elements per row at `source.stride(0)`
+    for both). `indices` is int32 or int64, `indicator` uint16 per row. Runs on the current
+    stream of the tensors' device; indices outside the rows are skipped."""
+    _require(source.is_cuda and target.is_cuda and indices.is_cuda and indicator.is_cuda,
+             "source, target, indices and indicator must be CUDA tensors")
+    _require(source.shape == target.shape and source.dtype == target.dtype, "source and target must match in shape and dtype")
+    _require(source.dim() >= 1 and source.stride(0) == target.stride(0), "source and target must share the row stride")
+    rows = source.size(0)
+    if rows == 0 or indices.numel() == 0:
+        return
+    _require(source[0].is_contiguous() and target[0].is_contiguous(), "rows must be contiguous")
+    _require(indicator.dtype == torch.uint16 and indicator.is_contiguous() and indicator.numel() >= rows,
+             "indicator must be a contiguous uint16 tensor with an entry per row")
+    _require(indices.dim() == 1 and indices.is_contiguous(), "indices must be a contiguous vector")
+    cols = source[0].numel()
+    lib = _abi.load_library()
+    with torch.cuda.device(source.device):
+        _abi.check(lib.sonic_indexed_copy(
+            ctypes.c_void_p(source.data_ptr()), ctypes.c_void_p(target.data_ptr()), rows, source.stride(0), cols,
+            source.element_size(), ctypes.c_void_p(indices.data_ptr()), index_dtype(indices, "indices"),
+            indices.numel(), ctypes.c_void_p(indicator.data_ptr()), ctypes.c_void_p(_stream(source.device))), lib)

@@ -286,7 +286,31 @@ def case_multistep_varlen():
                     greedy_slots=(3,), varlen_lengths=[2, 4, 1, 3])
 
 
+def case_indexed_copy():
+    """The reference's noise staging kernel (ops/copy.py:21-127) on [slots, T, V] bf16 noise:
+    a row that fits one block, and rows of several 8192-column blocks with a ragged last one."""
+    import sonic_sampler.ops.copy as ref_copy
+
+    ref_copy.total_sm = lambda device: 148  # no GPU here: the grid rule's SM count
+    inputs, outputs = {}, {}
+    for tag, (slots, steps, vocab) in {"small": (6, 3, 1000), "blocks": (5, 2, 8192 + 4100)}.items():
+        g = gen(7 + slots)
+        source = torch.randn(slots, steps, vocab, generator=g).to(BF16)
+        target = torch.randn(slots, steps, vocab, generator=g).to(BF16)
+        indices = torch.randperm(slots, generator=g)[: slots - 1].to(torch.int64)
+        indicator = torch.zeros(slots, dtype=torch.uint16)
+        indicator[indices[1]] = 0x40  # a greedy slot: not staged
+        indicator[indices[2]] = 0x41  # greedy with another bit
+        indicator[indices[3]] = 0x3F  # every bit below greedy: staged
+        inputs[tag] = dict(source=source.clone(), target=target.clone(), indices=indices.clone(),
+                           indicator=indicator.clone())
+        ref_copy.indexed_copy(source, target, indices, indicator)
+        outputs[tag] = dict(target=target.clone())
+    save("indexed_copy", inputs, outputs, {"reference": "ops/copy.py:21-127 indexed_copy"})
+
+
 CASES = {
+    "indexed_copy": case_indexed_copy,
     "topk_bf16": case_topk_bf16,
     "topk_bitonic": case_topk_bitonic,
     "singular_mixed": case_singular_mixed,

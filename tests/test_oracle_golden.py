@@ -129,3 +129,15 @@ def test_multistep(oracle_lib, name):
                                   return_logprobs=True, logprobs_dtype=F32, **kw)
     oracle_lib.fused_multistep(args)
     assert check_multistep(ver, kw, case) > 0
+
+
+@pytest.mark.parametrize("tag", ["small", "blocks"])
+def test_indexed_copy(tag):
+    """The oracle's noise staging against the reference kernel's own output (bit for bit)."""
+    from oracle import oracle
+
+    case = load("indexed_copy")
+    i, o = case["inputs"][tag], case["outputs"][tag]
+    target = i["target"].clone()
+    oracle.indexed_copy(i["source"], target, i["indices"], i["indicator"])
+    assert torch.equal(target.view(torch.int16), o["target"].view(torch.int16))
