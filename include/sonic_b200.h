@@ -36,7 +36,7 @@
 extern "C" {
 #endif
 
-#define SONIC_B200_ABI_VERSION 1
+#define SONIC_B200_ABI_VERSION 2
 
 /* Candidate-set width of the two-stage top-k (reference ops/base.py:24, MAX_K). */
 #define SONIC_MAX_K 128
@@ -66,7 +66,7 @@ enum {
   SONIC_FLAG_UPDATE_COUNTS = 1u << 2,  /* update decode counts with the selected tokens */
   SONIC_FLAG_LOGPROBS = 1u << 3,       /* write selected (and top-Z) logprobs */
   SONIC_FLAG_PROBABILITIES = 1u << 4,  /* singular: write candidate probabilities */
-  SONIC_FLAG_PHILOX = 1u << 5          /* singular: counter-based Philox Gumbel noise */
+  SONIC_FLAG_PHILOX = 1u << 5          /* counter-based Philox noise instead of the noise buffers */
 };
 
 /*
@@ -187,6 +187,15 @@ typedef struct SonicMultistepArgs {
 
   void* workspace;
   size_t workspace_bytes;
+
+  /* SONIC_FLAG_PHILOX (an addition of this library; the reference always reads buffers):
+   * `uniform` and `gumbel` are not read. Step s of the call draws with counter offset
+   * philox_offset + s under key philox_seed: the rejection step's log(Exp(1)) noise of token
+   * t from counter (t, slot, offset + s), in fp32; the acceptance uniform from counter
+   * (0xffffffff, slot, offset + s), rounded to bf16. Use distinct offsets for distinct calls,
+   * and for the drafting calls whose noise must differ (on-policy rejection sampling). */
+  uint64_t philox_seed;
+  uint64_t philox_offset;
 } SonicMultistepArgs;
 
 /*

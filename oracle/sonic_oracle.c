@@ -211,11 +211,21 @@ static void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
 
 /* log(Exp(1)) noise for (slot, token) in the counter-based mode: the same quantity the
    reference keeps in its Gumbel buffer (core/buffer.py:95-120), generated in fp32. */
-float ox_philox_log_exponential(uint64_t seed, uint64_t offset, int64_t slot, int64_t token) {
-  uint32_t c[4] = {(uint32_t)token, (uint32_t)slot, (uint32_t)offset, (uint32_t)(offset >> 32)};
+static float philox_unit(uint64_t seed, uint64_t offset, int64_t slot, uint32_t token) {
+  uint32_t c[4] = {token, (uint32_t)slot, (uint32_t)offset, (uint32_t)(offset >> 32)};
   philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
-  float u = ((float)(c[0] >> 9) + 0.5f) * (1.0f / 8388608.0f);
+  return ((float)(c[0] >> 9) + 0.5f) * (1.0f / 8388608.0f);
+}
+
+float ox_philox_log_exponential(uint64_t seed, uint64_t offset, int64_t slot, int64_t token) {
+  float u = philox_unit(seed, offset, slot, (uint32_t)token);
   return ox_log(-ox_log(u));
+}
+
+/* Counter-based acceptance uniform of a multistep step (an addition of this library: the
+   reference reads its bf16 uniform buffer): token word 0xffffffff, rounded to bf16. */
+static float ox_philox_acceptance(uint64_t seed, uint64_t offset, int64_t slot) {
+  return rbf(philox_unit(seed, offset, slot, 0xffffffffu));
 }
 
 /* ------------------------------------------------------------------------------------ */
@@ -541,7 +551,8 @@ sonic_status oracle_fused_multistep(const SonicMultistepArgs* a) {
       }
       const int stochastic_draft = a->draft_probs && !(ind & 0x800);
       for (accepted = 0; accepted < T - 1; ++accepted) {
-        float u = bf2f(a->uniform[slot * a->uniform_stride + accepted]);
+        float u = (a->flags & SONIC_FLAG_PHILOX) ? ox_philox_acceptance(a->philox_seed, a->philox_offset + accepted, slot)
+                                                 : bf2f(a->uniform[slot * a->uniform_stride + accepted]);
         if (stochastic_draft) {
           int64_t qi = slot * a->draft_stride + accepted * a->draft_step_stride + dr[accepted];
           if (a->draft_dtype == SONIC_DTYPE_F32)
@@ -566,7 +577,9 @@ sonic_status oracle_fused_multistep(const SonicMultistepArgs* a) {
           r = sc - q;
           r = r < 0.0f ? 0.0f : (r > 1.0f ? 1.0f : r);
         }
-        float g = bf2f(a->gumbel[slot * a->gumbel_stride + accepted * a->gumbel_step_stride + cand[accepted][i]]);
+        float g = (a->flags & SONIC_FLAG_PHILOX)
+                      ? ox_philox_log_exponential(a->philox_seed, a->philox_offset + accepted, slot, cand[accepted][i])
+                      : bf2f(a->gumbel[slot * a->gumbel_stride + accepted * a->gumbel_step_stride + cand[accepted][i]]);
         score[i] = ox_log(r) - g;
         res[i] = r;
       }

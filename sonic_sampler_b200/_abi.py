@@ -12,7 +12,7 @@ import ctypes
 import os
 from pathlib import Path
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 MAX_K = 128
 MAX_LOOKAHEAD = 15
 
@@ -142,6 +142,8 @@ class MultistepArgs(ctypes.Structure):
         ("top_stride", _i64),
         ("workspace", _vp),
         ("workspace_bytes", ctypes.c_size_t),
+        ("philox_seed", ctypes.c_uint64),
+        ("philox_offset", ctypes.c_uint64),
     ]
 
 

@@ -116,11 +116,11 @@ __device__ __forceinline__ float dlog(float x) {
 
 // ---------------------------------------------------------------------------------------
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw: "Parallel random numbers: as easy as 1, 2, 3",
-// SC'11): counter (token, slot, offset) under key `seed` -> log(Exp(1)) noise in fp32.
+// SC'11): counter (token, slot, offset) under key `seed` -> one 32-bit word, turned into
+// log(Exp(1)) noise (per token) or an acceptance uniform (token word 0xffffffff).
 // ---------------------------------------------------------------------------------------
 
-__device__ __forceinline__ float philox_log_exponential(uint64_t seed, uint64_t offset, uint32_t slot,
-                                                        uint32_t token) {
+__device__ __forceinline__ uint32_t philox_word(uint64_t seed, uint64_t offset, uint32_t slot, uint32_t token) {
   uint32_t c0 = token, c1 = slot, c2 = (uint32_t)offset, c3 = (uint32_t)(offset >> 32);
   uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
 #pragma unroll
@@ -135,8 +135,23 @@ __device__ __forceinline__ float philox_log_exponential(uint64_t seed, uint64_t 
     k0 += 0x9E3779B9u;
     k1 += 0xBB67AE85u;
   }
-  float u = __fmul_rn(__fadd_rn((float)(c0 >> 9), 0.5f), 1.0f / 8388608.0f);
-  return dlog(-dlog(u));
+  return c0;
+}
+
+// a uniform draw in (0, 1): the word's top 23 bits, centred in their interval
+__device__ __forceinline__ float philox_unit(uint32_t w) {
+  return __fmul_rn(__fadd_rn((float)(w >> 9), 0.5f), 1.0f / 8388608.0f);
+}
+
+__device__ __forceinline__ float philox_log_exponential(uint64_t seed, uint64_t offset, uint32_t slot,
+                                                        uint32_t token) {
+  return dlog(-dlog(philox_unit(philox_word(seed, offset, slot, token))));
+}
+
+// acceptance uniform of a multistep slot (counter offset = the call's offset + step): the
+// bf16 value of a (0, 1) draw, as the reference keeps its uniforms in bf16
+__device__ __forceinline__ float philox_acceptance(uint64_t seed, uint64_t offset, uint32_t slot) {
+  return rbf(philox_unit(philox_word(seed, offset, slot, 0xffffffffu)));
 }
 
 // ---------------------------------------------------------------------------------------

@@ -1949,7 +1949,8 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
     sm.drafted[tid] = d;
     // the acceptance loop's per-step inputs, loaded once and in parallel
     if (!greedy && tid < T - 1) {
-      sm.u[tid] = bf2f(a.uniform[slot * a.uniform_stride + tid]);
+      sm.u[tid] = (a.flags & SONIC_FLAG_PHILOX) ? philox_acceptance(a.philox_seed, a.philox_offset + tid, (uint32_t)slot)
+                                                : bf2f(a.uniform[slot * a.uniform_stride + tid]);
       float q = 1.0f;
       if (stochastic_q && d >= 0 && d < a.vocab_size) {
         const int64_t qi = slot * a.draft_stride + tid * a.draft_step_stride + d;
@@ -1983,7 +1984,8 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (idx[j] < 0 || idx[j] >= a.vocab_size) continue;
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + s * a.gumbel_step_stride + idx[j]));
+        if (!(a.flags & SONIC_FLAG_PHILOX))
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + s * a.gumbel_step_stride + idx[j]));
         if (stochastic_q && s < T - 1) {
           const int64_t qi = slot * a.draft_stride + s * a.draft_step_stride + idx[j];
           asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.draft_probs +
@@ -2076,7 +2078,11 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
         rr = __fsub_rn(sc, q);
         rr = rr < 0.0f ? 0.0f : (rr > 1.0f ? 1.0f : rr);
       }
-      const float g = bad ? 0.0f : bf2f(a.gumbel[slot * a.gumbel_stride + accepted * a.gumbel_step_stride + pos[j]]);
+      const float g = bad ? 0.0f
+                          : (flags & SONIC_FLAG_PHILOX)
+                                ? philox_log_exponential(a.philox_seed, a.philox_offset + accepted, (uint32_t)slot,
+                                                         (uint32_t)pos[j])
+                                : bf2f(a.gumbel[slot * a.gumbel_stride + accepted * a.gumbel_step_stride + pos[j]]);
       score[j] = __fsub_rn(dlog(rr), g);
     }
     const int sel = warp_argmax128(score, lane);
@@ -2377,7 +2383,8 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
     return fail(SONIC_ERR_INVALID_ARGUMENT, "logits must be a non-NULL bf16 tensor");
   if (!a->drafted_tokens || !a->tokens || !a->offsets)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "drafted_tokens, tokens and offsets must not be NULL");
-  if (!a->gumbel || !a->uniform) return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel and uniform noise must not be NULL");
+  if (!(a->flags & SONIC_FLAG_PHILOX) && (!a->gumbel || !a->uniform))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "gumbel and uniform noise must not be NULL without SONIC_FLAG_PHILOX");
   if (a->draft_probs && a->draft_dtype != SONIC_DTYPE_F32 && a->draft_dtype != SONIC_DTYPE_BF16)
     return fail(SONIC_ERR_INVALID_ARGUMENT, "draft probabilities dtype must be f32 or bf16");
   if ((a->flags & SONIC_FLAG_UPDATE_COUNTS) && !a->params.decode_counts)

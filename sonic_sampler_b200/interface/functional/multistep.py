@@ -2,8 +2,12 @@
 (reference interface/functional/multistep.py:175-461).
 
 Same keyword set, shape handling and ValueErrors as the reference; the three Triton
-launches become one launch of the fused B200 kernel (`sonic_fused_multistep`), which also
-reads each request's count and bias rows once instead of once per timestep.
+launches become the fused B200 kernels of `sonic_fused_multistep`, which also read each
+request's count and bias rows once instead of once per timestep.
+
+One addition, off by default: `philox_seed` / `philox_offset` draw the acceptance uniforms
+and the rejection step's Gumbel noise in-kernel from counter-based Philox (step s of the
+call uses counter offset `philox_offset + s`), so no noise buffer is read or refreshed.
 """
 
 from __future__ import annotations
@@ -12,7 +16,7 @@ import torch
 from torch import Tensor
 
 from sonic_sampler_b200 import ops
-from sonic_sampler_b200._abi import FLAG_LOGPROBS, FLAG_PDL, FLAG_UPDATE_COUNTS, MAX_K
+from sonic_sampler_b200._abi import FLAG_LOGPROBS, FLAG_PDL, FLAG_PHILOX, FLAG_UPDATE_COUNTS, MAX_K
 from sonic_sampler_b200.base.sampler import DEFAULT_TOP_LOGPROBS, Verification
 from sonic_sampler_b200.interface.base import TopKStrategy
 from sonic_sampler_b200.interface.dispatch import ThreeStageWarpConfig
@@ -118,6 +122,9 @@ def prepare_multistep(
     top_k_logprobs: Tensor | None = None,
     gumbel_noise: Tensor | None = None,
     uniform_noise: Tensor | None = None,
+    # Counter-based in-kernel noise (B200 addition; see module docstring).
+    philox_seed: int | None = None,
+    philox_offset: int = 0,
     # Output Buffer(s).
     output_tokens: Tensor | None = None,
     # Top-K Strategy & Tuning Configuration (accepted; no effect on the B200 kernel).
@@ -139,8 +146,11 @@ def prepare_multistep(
 
     flat_logits = collapse_2d(logits)
     values_buffer, indices_buffer = resolve_unpack_buffers(logits, values, indices)
-    gumbel_weights = resolve_gumbel(gumbel_noise, logits, batch_size, gamma + 1)
-    uniform_weights = resolve_uniform(uniform_noise, logits, batch_size, gamma)
+    philox = philox_seed is not None
+    # with Philox noise no buffer is read, so none is drawn either (the reference's default
+    # draws fresh [B, gamma+1, V] and [B, gamma] buffers on every call)
+    gumbel_weights = None if philox else resolve_gumbel(gumbel_noise, logits, batch_size, gamma + 1)
+    uniform_weights = None if philox else resolve_uniform(uniform_noise, logits, batch_size, gamma)
 
     verification = Verification.from_tokens(
         tokens=resolve_tokens(drafted_tokens, output_tokens), batch_size=batch_size, timesteps=gamma + 1,
@@ -156,9 +166,15 @@ def prepare_multistep(
         (FLAG_PDL if enable_pdl else 0)
         | (FLAG_UPDATE_COUNTS if update_counts else 0)
         | (FLAG_LOGPROBS if return_logprobs else 0)
+        | (FLAG_PHILOX if philox else 0)
     )
-    # counts and bias rows are read with the noise row stride (functional/multistep.py:316)
-    stride_c = collapse_2d(gumbel_weights).stride(0)
+    # counts and bias rows are read with the noise row stride (functional/multistep.py:316);
+    # without a noise buffer, with their own row stride
+    if gumbel_weights is not None:
+        stride_c = collapse_2d(gumbel_weights).stride(0)
+    else:
+        rows_c = [t for t in (decode_counts, context_counts, logit_bias, draft_probabilities) if t is not None]
+        stride_c = collapse_2d(rows_c[0]).stride(0) if rows_c else vocab_size
     params = ops.sampling_params(
         indicators, slot_mapping=slot_mapping, grammar=grammar,
         grammar_stride=None if grammar is None else collapse_2d(grammar).stride(0),
@@ -181,6 +197,7 @@ def prepare_multistep(
         draft_step_stride=stride_c,
         values=values_buffer, indices=indices_buffer, logprobs=token_logprobs,
         top_logprob_values=top_logprobs, top_logprob_tokens=top_tokens, workspace=workspace,
+        philox_seed=philox_seed or 0, philox_offset=philox_offset,
     )
     return verification, args
 

@@ -205,8 +205,8 @@ def multistep_args(
     drafted_tokens: Tensor,
     tokens: Tensor,
     offsets: Tensor,
-    uniform: Tensor,
-    gumbel: Tensor,
+    uniform: Tensor | None,
+    gumbel: Tensor | None,
     gumbel_step_stride: int,
     flags: int,
     cu_seqlens: Tensor | None = None,
@@ -220,6 +220,8 @@ def multistep_args(
     top_logprob_values: Tensor | None = None,
     top_logprob_tokens: Tensor | None = None,
     workspace: Tensor | None = None,
+    philox_seed: int = 0,
+    philox_offset: int = 0,
 ) -> MultistepArgs:
     a = MultistepArgs()
     _require(logits.dim() == 2, "logits must be collapsed to 2-D [rows, vocab]")
@@ -245,9 +247,13 @@ def multistep_args(
         a.draft_dtype = _FLOAT_DTYPES[draft_probs.dtype]
         a.draft_stride = draft_probs.stride(0)
         a.draft_step_stride = draft_step_stride
-    a.uniform, a.uniform_stride = _rows(uniform, "uniform_noise", (BF16,))
-    a.gumbel, a.gumbel_stride = _rows(gumbel, "gumbel_noise", (BF16,))
+    if uniform is not None:
+        a.uniform, a.uniform_stride = _rows(uniform, "uniform_noise", (BF16,))
+    if gumbel is not None:
+        a.gumbel, a.gumbel_stride = _rows(gumbel, "gumbel_noise", (BF16,))
     a.gumbel_step_stride = gumbel_step_stride
+    a.philox_seed = philox_seed & 0xFFFFFFFFFFFFFFFF
+    a.philox_offset = philox_offset & 0xFFFFFFFFFFFFFFFF
     if values is not None:
         _require(values.dtype == F32 and values.is_contiguous(), "values buffer must be contiguous fp32")
         a.values = values.data_ptr()

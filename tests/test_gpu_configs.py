@@ -579,3 +579,52 @@ def test_topk_small_k_with_ties(dev, k):
     oracle.bounded_topk(ops.topk_args(x.cpu(), vocab_size=vocab, k=k, block_n=topk.block_n, values=hv, indices=hi))
     assert torch.equal(idx, hi.view(rows, k))
     assert torch.equal(bits(vals), bits(hv.view(rows, k)))
+
+
+# ----------------------------------------------------------------------------------------
+# multistep with counter-based (Philox) noise
+# ----------------------------------------------------------------------------------------
+
+
+def test_multistep_philox_matches_oracle(dev):
+    """Config-3 shapes with in-kernel acceptance uniforms and rejection noise: tokens,
+    offsets, counts and logprobs equal the oracle's (which draws the same counters)."""
+    w = workloads.config3(dev, seed=11)
+    kw = buffer_kwargs(w["buffers"], timestep=None)
+    kw.pop("gumbel_noise")
+    kw.pop("uniform_noise")
+    ver, ref, kw, kh = run_multistep(w["flat_logits"], w["flat_tokens"], cu_seqlens=w["cu_seqlens"],
+                                     lookahead=w["gamma"], max_top_logprobs=20, update_counts=True,
+                                     return_logprobs=True, draft_probabilities=w["probabilities"], block_n=4096,
+                                     philox_seed=97, philox_offset=5, **kw)
+    cu = w["cu_seqlens"].cpu().tolist()
+    _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(32)), cu[:-1])
+
+
+def test_multistep_philox_residual_distribution(dev):
+    """Every draft is rejected (its token is outside the row's candidates), so the token is
+    drawn from the residual, here the target's top-8 softmax: the counts over many requests
+    pass a chi-squared test, and every offset is 0."""
+    from sonic_sampler_b200.interface.functional.multistep import fused_multistep
+
+    requests, vocab = 4096, 4096
+    g = torch.Generator().manual_seed(12)
+    row = torch.full((vocab,), -30.0)
+    support = torch.randperm(vocab, generator=g)[:8]
+    row[support] = torch.tensor([2.0, 1.5, 1.0, 0.5, 0.0, -0.5, -1.0, -1.5])
+    # gamma = 1: rows (step 0, bonus step) of every request; the drafted token is never a candidate
+    logits = row.to(BF16).to(dev).expand(requests * 2, vocab).contiguous()
+    outside = int(torch.topk(row, 200, largest=False).indices[0])
+    drafted = torch.full((requests * 2,), outside, dtype=I32, device=dev)
+    ind = torch.full((requests,), 0x80, dtype=torch.uint16, device=dev)
+    top_k = torch.full((requests,), 8, dtype=I32, device=dev)
+    ver = fused_multistep(logits, ind, drafted, lookahead=1, top_k=top_k, block_n=1024, philox_seed=4321)
+    torch.cuda.synchronize()
+    assert int(ver.offsets.abs().max()) == 0
+    toks = ver.tokens.view(requests, 2)[:, 0].cpu()
+    assert bool(torch.isin(toks, support).all())
+    p = torch.softmax(row.to(BF16).float()[support], 0)
+    counts = torch.stack([(toks == t).sum() for t in support]).double()
+    expected = p.double() * requests
+    chi2 = float(((counts - expected) ** 2 / expected).sum())
+    assert chi2 < 24.32, (chi2, counts.tolist(), expected.tolist())  # 7 dof, P = 0.001
