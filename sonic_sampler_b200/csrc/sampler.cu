@@ -1024,14 +1024,39 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   pdl_wait();
 
+  // Chunk 0's logits sit at offset 0 of stage 0 in every stage layout: that copy goes out
+  // before the row's parameters are loaded (its bytes are expected without an arrival; the
+  // arrival comes with the row's other streams, or on the way out).
+  const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
+  const int nch = MODE == kTma ? (int)((c1 - c0) / CH) : 0;
+  if (nch > 0 && tid == 0) {
+    for (int i = 0; i < MAX_RING_STAGES; ++i) {
+      mbar_init(&st.bars[i], 1);
+      st.rel[i] = 0;
+    }
+    mbar_fence_init();
+    mbar_expect_tx_only(&st.bars[0], CH * 2);
+    bulk_load(smem_ring, xrow + c0, CH * 2, &st.bars[0]);
+  }
+  auto drain = [&]() {  // leaving early: the copy lands before the CTA does
+    if (nch > 0 && tid == 0) {
+      mbar_arrive(&st.bars[0]);
+      mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT);
+    }
+  };
+
   // MS: row r is step `step` of multistep request `req` (rows [margin, margin + T))
   int64_t req = r, margin = 0;
   int step = 0;
-  if (MS && !ms_row(ms, r, req, step, margin)) return;
+  if (MS && !ms_row(ms, r, req, step, margin)) {
+    drain();
+    return;
+  }
   const int64_t slot = load_slot(P, req);
   if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
     // out-of-range slot id: no CTA of this row touches per-slot buffers or the ticket
     if (!MS && split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
+    drain();
     return;
   }
   const uint32_t ind = P.indicators[slot];
@@ -1048,7 +1073,6 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const int64_t gslot = MS ? slot * (ms.lookahead + 1) + step : slot;
   // streams of the bulk-copy ring (see below)
   const int64_t shard = a.shard_offset;
-  const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
   const uint32_t* grow = rc.nd.g ? P.grammar + gslot * P.grammar_stride : nullptr;
   const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
   const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
@@ -1064,8 +1088,14 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     unsigned char* sp = smem_ring + stage * sg_stage;
     uint64_t* bar = &st.bars[stage];
     const int64_t cc = c0 + (int64_t)i * CH;
-    mbar_expect_tx(bar, (uint32_t)sg_stage);
-    bulk_load(sp, xrow + cc, CH * 2, bar);
+    if (i == 0) {
+      // the logits are on their way already
+      if (sg_stage > CH * 2) mbar_expect_tx(bar, (uint32_t)(sg_stage - CH * 2));
+      else mbar_arrive(bar);
+    } else {
+      mbar_expect_tx(bar, (uint32_t)sg_stage);
+      bulk_load(sp, xrow + cc, CH * 2, bar);
+    }
     if (drow) bulk_load(sp + sg_d, drow + cc + shard, CH * 4, bar);
     if (crow) bulk_load(sp + sg_c, crow + cc + shard, CH * 4, bar);
     if (brow) bulk_load(sp + sg_b, brow + cc + shard, CH * 2, bar);
@@ -1075,15 +1105,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     st.best = 0ull;
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
-    if (MODE == kTma) {
-      for (int i = 0; i < nst; ++i) {
-        mbar_init(&st.bars[i], 1);
-        st.rel[i] = 0;
-      }
-      mbar_fence_init();
-      const int nch = (int)((c1 - c0) / CH);
-      for (int i = 0; i < min(nch, nst); ++i) issue_chunk(i, i);
-    }
+    for (int i = 0; i < min(nch, nst); ++i) issue_chunk(i, i);  // barriers set up above
   }
   __syncthreads();
 
@@ -1467,16 +1489,8 @@ __global__ void __launch_bounds__(NT, 3) plain_kernel(const SonicSingularArgs a,
 
   pdl_wait();
 
-  const int64_t slot = load_slot(P, r);
-  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
-    if (split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
-    return;
-  }
-  const uint32_t ind = P.indicators[slot];
-  const RowConsts rc = row_consts(P, slot, ind);
-  const bool greedy = (ind & 0x40) != 0;
-  const int kk = needed_candidates(a, ind, slot, false);  // exact leading candidates needed
-  const int mm = (kk + NW - 1) / NW;                      // of them per warp (cut rules)
+  // The ring's addresses depend on the row alone: its first stages go out before the row's
+  // parameters are loaded, so the copies overlap that chain of dependent loads.
   const uint16_t* xrow = (const uint16_t*)a.logits + r * a.logits_stride;
   const int nchunks = MODE == kTma ? (int)((c1 - c0) / PCH) : 0;
   auto issue_chunk = [&](int i, int stage) {  // one thread
@@ -1484,18 +1498,32 @@ __global__ void __launch_bounds__(NT, 3) plain_kernel(const SonicSingularArgs a,
     mbar_expect_tx(bar, (uint32_t)PSTAGE);
     bulk_load(smem_ring + stage * PSTAGE, xrow + c0 + (int64_t)i * PCH, PSTAGE, bar);
   };
+  if (MODE == kTma && tid == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&st.bars[i], 1);
+      st.rel[i] = 0;
+    }
+    mbar_fence_init();
+    for (int i = 0; i < min(nchunks, nst); ++i) issue_chunk(i, i);
+  }
+
+  const int64_t slot = load_slot(P, r);
+  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
+    if (split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
+    // the copies already issued land before the CTA leaves
+    if (MODE == kTma && tid == 0)
+      for (int i = 0; i < min(nchunks, nst); ++i) mbar_wait_bounded(&st.bars[i], 0u, WAIT_LIMIT);
+    return;
+  }
+  const uint32_t ind = P.indicators[slot];
+  const RowConsts rc = row_consts(P, slot, ind);
+  const bool greedy = (ind & 0x40) != 0;
+  const int kk = needed_candidates(a, ind, slot, false);  // exact leading candidates needed
+  const int mm = (kk + NW - 1) / NW;                      // of them per warp (cut rules)
   if (tid == 0) {
     st.best = 0ull;
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
-    if (MODE == kTma) {
-      for (int i = 0; i < nst; ++i) {
-        mbar_init(&st.bars[i], 1);
-        st.rel[i] = 0;
-      }
-      mbar_fence_init();
-      for (int i = 0; i < min(nchunks, nst); ++i) issue_chunk(i, i);
-    }
   }
   __syncthreads();
 
@@ -2476,10 +2504,6 @@ __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.comm
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 // every committed bulk store has completed
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 __global__ void __launch_bounds__(32) indexed_copy_kernel(const CopyArgs c, int64_t chunks_per_row, int64_t total) {
   extern __shared__ __align__(128) unsigned char ring[];
   __shared__ uint64_t bars[CP_STAGES];
