@@ -444,6 +444,7 @@ __device__ __forceinline__ void decode_keys(const uint64_t (&k)[4], float (&v)[4
 struct MaskParams {
   int32_t top_k, top_logprobs;
   uint16_t top_p, min_p;
+  float log_min_p;  // log(min_p), computed once with the parameters
   bool has_k, has_p, has_min_p;
 };
 
@@ -456,6 +457,7 @@ __device__ __forceinline__ MaskParams load_mask_params(const SonicSamplingParams
   m.top_p = m.has_p ? P.top_p[slot] : 0;
   m.min_p = m.has_min_p ? P.min_p[slot] : 0;
   m.top_logprobs = P.top_logprobs ? P.top_logprobs[slot] : 0;
+  m.log_min_p = m.has_min_p ? dlog(bf2f(m.min_p)) : 0.0f;
   return m;
 }
 
@@ -484,7 +486,7 @@ __device__ __forceinline__ bool warp_masking(const MaskParams& M, uint32_t ind, 
       if (!(lad[j] <= scale || (lane == 0 && j == 0))) v[j] = ninf;
   }
   if ((ind & 0x200) && M.has_min_p) {
-    const float pivot = __fadd_rn(dlog(bf2f(M.min_p)), maximum);
+    const float pivot = __fadd_rn(M.log_min_p, maximum);
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (!(v[j] >= pivot)) v[j] = ninf;
@@ -973,7 +975,8 @@ __device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r
   const int64_t token = warp_pick128(tok, sel);
   if (lane == 0 && (flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
     int32_t* d = P.decode_counts + slot * P.counts_stride + token;
-    *d = (flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+    if (flags & SONIC_FLAG_PREFILL) *d = 1;
+    else atomicAdd(d, 1);
   }
   if (flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
     float ls[4];
@@ -1415,7 +1418,8 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     if (lane == 0) {
       if ((flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
         int32_t* d = P.decode_counts + slot * P.counts_stride + token;
-        *d = (flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+        if (flags & SONIC_FLAG_PREFILL) *d = 1;
+        else atomicAdd(d, 1);
       }
       a.tokens[r * a.tokens_stride] = (int32_t)token;
     }
@@ -1765,7 +1769,8 @@ __global__ void __launch_bounds__(NT) merge_candidates_kernel(const SonicSingula
     if (lane == 0) {
       if ((a.flags & SONIC_FLAG_UPDATE_COUNTS) && token >= 0 && token < P.counts_stride) {
         int32_t* d = P.decode_counts + slot * P.counts_stride + token;
-        *d = (a.flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+        if (a.flags & SONIC_FLAG_PREFILL) *d = 1;
+        else atomicAdd(d, 1);
       }
       a.tokens[r * a.tokens_stride] = (int32_t)token;
     }
