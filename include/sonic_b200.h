@@ -25,6 +25,9 @@
  *                             chain_speculative_verification_kernel)
  *   sonic_bounded_topk     <- interface/topk.py:98-161 (UnshardedBoundedTopK.__call__:
  *                             ops/topk/bitpack.py:99 + ops/topk/unpack.py:312)
+ *   sonic_indexed_copy     <- ops/copy.py:21-127 (indexed_copy, noise staging)
+ *   sonic_populate_slots   <- core/buffer.py:1026-1052, 1098-1352 (SamplingBuffers
+ *                             step_grammar / transfer / update / allocate, host population)
  */
 #ifndef SONIC_B200_H
 #define SONIC_B200_H
@@ -36,7 +39,7 @@
 extern "C" {
 #endif
 
-#define SONIC_B200_ABI_VERSION 2
+#define SONIC_B200_ABI_VERSION 3
 
 /* Candidate-set width of the two-stage top-k (reference ops/base.py:24, MAX_K). */
 #define SONIC_MAX_K 128
@@ -273,6 +276,89 @@ sonic_status sonic_fused_singular_static(const SonicSingularArgs* args, void* st
 sonic_status sonic_indexed_copy(const void* source, void* target, int64_t rows, int64_t stride, int64_t cols,
                                 int32_t elem_bytes, const void* indices, int32_t index_dtype, int32_t count,
                                 const uint16_t* indicator, void* stream);
+
+/* Parts of the slot buffers sonic_populate_slots writes (SonicPopulateArgs.parts). */
+enum {
+  SONIC_POPULATE_SCALARS = 0x1,      /* temperature, top_p, min_p, top_k, top_logprobs, the three
+                                        repetition penalties and the target/draft indicators */
+  SONIC_POPULATE_HISTOGRAM = 0x2,    /* context counts = histogram of the slot's prompt tokens,
+                                        decode counts = 0 (admission) */
+  SONIC_POPULATE_DENSE_COUNTS = 0x4, /* context and decode counts copied from dense rows */
+  SONIC_POPULATE_BIAS = 0x8,         /* bias row = 0, then the slot's (token, value) entries */
+  SONIC_POPULATE_GRAMMAR = 0x10      /* grammar words of the slots that carry a bitmask */
+};
+
+/* One batched population of request slots (sonic_populate_slots). Every input array is device
+ * memory (normally one staged blob copied from pinned host memory with one cudaMemcpyAsync);
+ * the destinations are the slot buffers the sampler reads (layout as SonicSamplingParams:
+ * bf16 scalars, i32 counts [num_slots][counts_stride], bf16 bias [num_slots][bias_stride],
+ * u32 grammar words). Slot i of the call is buffer row positions[i]. */
+typedef struct SonicPopulateArgs {
+  int32_t count;        /* slots in this call */
+  int32_t num_slots;    /* rows of the slot buffers; positions outside [0, num_slots) are skipped */
+  int64_t vocab_size;   /* V: columns of the count and bias rows */
+  uint32_t parts;       /* SONIC_POPULATE_* */
+  int32_t timesteps;    /* T: grammar steps of a slot */
+  int32_t grammar_step; /* >= 0: the bitmask goes to that step only (admission: 0);
+                           -1: to every step (one row broadcast, or T rows) */
+  int32_t _pad0;
+
+  const int32_t* positions;    /* [count] slot ids, distinct */
+  /* SONIC_POPULATE_SCALARS */
+  const uint16_t* values_bf16; /* [count][6] temperature, top_p, min_p, multiplicative,
+                                  frequency, presence (bf16 bits) */
+  const int32_t* values_i32;   /* [count][2] top_k, top_logprobs */
+  const uint16_t* indicators;  /* [count][2] target, draft */
+  /* SONIC_POPULATE_HISTOGRAM: tokens of slot i are tokens[token_offsets[i] .. token_offsets[i+1]);
+     ids outside [0, V) are not counted */
+  const int64_t* token_offsets;
+  const int32_t* tokens;
+  /* SONIC_POPULATE_DENSE_COUNTS: rows i of [count][V] */
+  const int32_t* dense_context;
+  const int32_t* dense_decode;
+  /* SONIC_POPULATE_BIAS: entries of slot i are [bias_offsets[i], bias_offsets[i+1]) of
+     bias_tokens / bias_values (bf16 bits); tokens distinct within a slot; NULL offsets = no
+     entries (rows zeroed) */
+  const int64_t* bias_offsets;
+  const int32_t* bias_tokens;
+  const uint16_t* bias_values;
+  /* SONIC_POPULATE_GRAMMAR: slot i's bitmask starts at row grammar_rows[i] (-1: none) of
+     grammar_words [rows][ceil(V / 32)] and has grammar_steps[i] rows (1, or T when
+     grammar_step is -1) */
+  const int32_t* grammar_rows;
+  const int32_t* grammar_steps;
+  const uint32_t* grammar_words;
+
+  /* destinations */
+  uint16_t* temperature;
+  uint16_t* top_p;
+  uint16_t* min_p;
+  int32_t* top_k;
+  int32_t* top_logprobs;
+  uint16_t* multiplicative;
+  uint16_t* frequency;
+  uint16_t* presence;
+  uint16_t* flags_target; /* element s: slot s's target indicator */
+  uint16_t* flags_draft;
+  int32_t* context_counts;
+  int32_t* decode_counts;
+  int64_t counts_stride;
+  uint16_t* bias;
+  int64_t bias_stride;
+  uint32_t* grammar;
+  int64_t grammar_slot_stride; /* words */
+  int64_t grammar_step_stride; /* words */
+} SonicPopulateArgs;
+
+/* Batched slot population: the device side of SamplingBuffers.allocate / update /
+ * step_grammar (core/buffer.py:1026-1052, 1098-1352). The reference issues a dozen
+ * `copy_` calls a slot through pinned memory (PinnedRelay.populate + transfer,
+ * RepetitionPenalties.populate + transfer, TokenCounts.allocate / update, Flags.update,
+ * step_grammar) and histograms the prompt on the host into a dense pinned row; this call
+ * writes the same values for every slot of the batch in one kernel launch from sparse
+ * inputs (prompt tokens, bias entries). Noise refresh stays with the caller's generator.
+ * Runs on `stream`, allocates nothing, never synchronises. */
+sonic_status sonic_populate_slots(const SonicPopulateArgs* args, void* stream);
 
 /* ABI version (SONIC_B200_ABI_VERSION) the library was built with. */
 int32_t sonic_abi_version(void);

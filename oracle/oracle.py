@@ -93,3 +93,63 @@ def indexed_copy(source, target, indices, indicator) -> None:
         j = int(indices[i])
         if not (int(indicator[j]) & 0x40):
             dst[j].copy_(src[j])
+
+
+def populate_slots(batch, dest: dict) -> None:
+    """CPU restatement of slot population from a packed call (the arrays of
+    sonic_populate_slots; `batch` is a core.population.SlotBatch). `dest` holds host tensors
+    named like the SamplingBuffers fields: temperature, top_p, min_p, top_k, top_logprobs,
+    multiplicative, frequency, presence, flags_target, flags_draft, context, decode, bias,
+    grammar [slots, T, W]. Updated in place, slot by slot, in the reference's terms:
+
+    - scalars and indicators: PinnedRelay.populate + transfer (core/buffer.py:738-764,
+      1098-1135), RepetitionPenalties.populate + transfer (:562-604), Flags.update
+      (core/flags.py:543-572);
+    - prompt histogram: pinned row zeroed and `scatter_add_` of ones at the prompt ids, copied to
+      the context counts; decode counts zeroed (TokenCounts.populate + allocate, :422-457);
+      dense counts copied (TokenCounts.update, :395-420);
+    - bias: row zeroed, then `scatter_` of the slot's values at its token ids
+      (PinnedRelay.update_bias, :707-736);
+    - grammar: `copy_` of the bitmask into step `grammar_step`, or into every step of the slot
+      (step_grammar, :1026-1052)."""
+    import torch
+
+    from sonic_sampler_b200.core import population as P
+
+    V = batch.vocab_size
+    bf = lambda a: torch.from_numpy(a.astype("int16")).view(torch.bfloat16)  # noqa: E731
+    for i in range(batch.count):
+        s = int(batch.positions[i])
+        if batch.parts & P.SCALARS:
+            f = bf(batch.values_bf16[i])
+            dest["temperature"][s], dest["top_p"][s], dest["min_p"][s] = f[0], f[1], f[2]
+            dest["multiplicative"][s], dest["frequency"][s], dest["presence"][s] = f[3], f[4], f[5]
+            dest["top_k"][s] = int(batch.values_i32[i, 0])
+            dest["top_logprobs"][s] = int(batch.values_i32[i, 1])
+            dest["flags_target"][s] = int(batch.indicators[i, 0])
+            dest["flags_draft"][s] = int(batch.indicators[i, 1])
+        if batch.parts & P.HISTOGRAM:
+            toks = torch.from_numpy(batch.tokens[batch.token_offsets[i]:batch.token_offsets[i + 1]].astype("int64"))
+            row = torch.zeros(V, dtype=torch.int32)
+            row.scatter_add_(0, toks, torch.ones_like(toks, dtype=torch.int32))
+            dest["context"][s, :V] = row
+            dest["decode"][s, :V] = 0
+        elif batch.parts & P.DENSE_COUNTS:
+            dc, dd = batch.dense_context, batch.dense_decode
+            dc = dc.cpu().numpy() if isinstance(dc, torch.Tensor) else dc
+            dd = dd.cpu().numpy() if isinstance(dd, torch.Tensor) else dd
+            dest["context"][s, :V] = torch.from_numpy(dc[i].copy())
+            dest["decode"][s, :V] = torch.from_numpy(dd[i].copy())
+        if batch.parts & P.BIAS:
+            row = torch.zeros(V, dtype=torch.bfloat16)
+            if batch.bias_offsets is not None:
+                b0, b1 = int(batch.bias_offsets[i]), int(batch.bias_offsets[i + 1])
+                row.scatter_(0, torch.from_numpy(batch.bias_tokens[b0:b1].astype("int64")),
+                             bf(batch.bias_values[b0:b1]))
+            dest["bias"][s, :V] = row
+        if batch.parts & P.GRAMMAR and int(batch.grammar_rows[i]) >= 0:
+            r0, n = int(batch.grammar_rows[i]), int(batch.grammar_steps[i])
+            g = dest["grammar"].view(torch.int32)
+            steps = [batch.grammar_step] if batch.grammar_step >= 0 else range(g.size(1))
+            for k, t in enumerate(steps):
+                g[s, t] = torch.from_numpy(batch.grammar_words[r0 + (k if n > 1 else 0)].view("int32").copy())

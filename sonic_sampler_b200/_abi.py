@@ -12,7 +12,7 @@ import ctypes
 import os
 from pathlib import Path
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 MAX_K = 128
 MAX_LOOKAHEAD = 15
 
@@ -36,6 +36,13 @@ FLAG_UPDATE_COUNTS = 1 << 2
 FLAG_LOGPROBS = 1 << 3
 FLAG_PROBABILITIES = 1 << 4
 FLAG_PHILOX = 1 << 5
+
+# parts of sonic_populate_slots
+POPULATE_SCALARS = 0x1
+POPULATE_HISTOGRAM = 0x2
+POPULATE_DENSE_COUNTS = 0x4
+POPULATE_BIAS = 0x8
+POPULATE_GRAMMAR = 0x10
 
 _vp = ctypes.c_void_p
 _i32 = ctypes.c_int32
@@ -166,6 +173,50 @@ class TopKArgs(ctypes.Structure):
     ]
 
 
+class PopulateArgs(ctypes.Structure):
+    _fields_ = [
+        ("count", _i32),
+        ("num_slots", _i32),
+        ("vocab_size", _i64),
+        ("parts", _u32),
+        ("timesteps", _i32),
+        ("grammar_step", _i32),
+        ("_pad0", _i32),
+        ("positions", _vp),
+        ("values_bf16", _vp),
+        ("values_i32", _vp),
+        ("indicators", _vp),
+        ("token_offsets", _vp),
+        ("tokens", _vp),
+        ("dense_context", _vp),
+        ("dense_decode", _vp),
+        ("bias_offsets", _vp),
+        ("bias_tokens", _vp),
+        ("bias_values", _vp),
+        ("grammar_rows", _vp),
+        ("grammar_steps", _vp),
+        ("grammar_words", _vp),
+        ("temperature", _vp),
+        ("top_p", _vp),
+        ("min_p", _vp),
+        ("top_k", _vp),
+        ("top_logprobs", _vp),
+        ("multiplicative", _vp),
+        ("frequency", _vp),
+        ("presence", _vp),
+        ("flags_target", _vp),
+        ("flags_draft", _vp),
+        ("context_counts", _vp),
+        ("decode_counts", _vp),
+        ("counts_stride", _i64),
+        ("bias", _vp),
+        ("bias_stride", _i64),
+        ("grammar", _vp),
+        ("grammar_slot_stride", _i64),
+        ("grammar_step_stride", _i64),
+    ]
+
+
 #: every symbol include/sonic_b200.h declares
 EXPORTED_SYMBOLS = (
     "sonic_fused_singular_workspace_size",
@@ -178,6 +229,7 @@ EXPORTED_SYMBOLS = (
     "sonic_shard_candidates",
     "sonic_merge_candidates",
     "sonic_indexed_copy",
+    "sonic_populate_slots",
     "sonic_abi_version",
     "sonic_last_error",
 )
@@ -211,6 +263,8 @@ def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
     lib.sonic_indexed_copy.argtypes = [_vp, _vp, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, _i32, _vp, _i32, _i32,
                                        _vp, _vp]
     lib.sonic_indexed_copy.restype = _i32
+    lib.sonic_populate_slots.argtypes = [ctypes.POINTER(PopulateArgs), _vp]
+    lib.sonic_populate_slots.restype = _i32
     lib.sonic_abi_version.argtypes = []
     lib.sonic_abi_version.restype = _i32
     lib.sonic_last_error.argtypes = []

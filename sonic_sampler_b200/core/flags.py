@@ -96,3 +96,59 @@ class Indicator(IntFlag):
 def indicator_tensor(values, device=None) -> torch.Tensor:
     """u16 indicator vector from a list of Indicator / ints."""
     return torch.tensor([int(v) for v in values], dtype=torch.uint16, device=device)
+
+
+class ScopedIndicators:
+    """Target and draft indicators of a list of slots (reference core/flags.py:229-432)."""
+
+    def __init__(self, target: list, draft: list):
+        self.target = [Indicator(int(v)) for v in target]
+        self.draft = [Indicator(int(v)) for v in draft]
+
+    @classmethod
+    def from_pairs(cls, pairs) -> "ScopedIndicators":
+        pairs = list(pairs)
+        return cls([t for t, _ in pairs], [d for _, d in pairs])
+
+    @classmethod
+    def from_params(cls, size: int, multiplicative=None, frequency=None, presence=None, biases=None,
+                    temperature=None, top_k=None, top_p=None, min_p=None, top_logprobs=None, bitmasks=None,
+                    greedy_drafts=False) -> "ScopedIndicators":
+        """Same resolution as the reference (core/flags.py:310-362), defaults included: a missing
+        or empty `temperature` list counts as 0.0 (which sets the temperature bit), and a bias
+        dict or bitmask that is not None sets its bit even when empty."""
+        if top_k and any(k > MAX_K for k in top_k):
+            raise ValueError(f"`top_k` greater than {MAX_K} is not supported")
+        fill = lambda v: [v] * size  # noqa: E731
+        drafter = list(greedy_drafts) if isinstance(greedy_drafts, list) else fill(greedy_drafts)
+        rows = zip(
+            [m is not None for m in bitmasks] if bitmasks else fill(False),
+            multiplicative or fill(1.0),
+            frequency or fill(0.0),
+            presence or fill(0.0),
+            [b is not None for b in biases] if biases else fill(False),
+            temperature or fill(0.0),
+            top_k or fill(MAX_K),
+            top_p or fill(1.0),
+            min_p or fill(0.0),
+            top_logprobs or fill(0),
+            drafter,
+        )
+        target = [Indicator.from_params(*r) for r in rows]
+        draft = [t.greedy() if g else t.disable(Indicator.TOP_K_LOGPROBS) for g, t in zip(drafter, target)]
+        return cls(target, draft)
+
+    @property
+    def has_stochastic_target(self) -> bool:
+        return any(not (v & Indicator.GREEDY) for v in self.target)
+
+    @property
+    def has_stochastic_draft(self) -> bool:
+        return any(not (v & Indicator.GREEDY) for v in self.draft)
+
+    @property
+    def stochastic_selectors(self) -> list[tuple[bool, bool]]:
+        return [(not (t & Indicator.GREEDY), not (d & Indicator.GREEDY)) for t, d in zip(self.target, self.draft)]
+
+    def subset(self, indices) -> "ScopedIndicators":
+        return ScopedIndicators([self.target[i] for i in indices], [self.draft[i] for i in indices])

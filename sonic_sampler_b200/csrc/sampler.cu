@@ -1479,8 +1479,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       for (int j = 0; j < 4; ++j) {
         const uint64_t key = to_global<uint32_t>(fin[j], c0);
         stcg64(out + 4 * lane + j, key);
-        // warm L2 with the noise the merge will gather for this candidate
-        if (key && !cand_out && !(a.flags & SONIC_FLAG_PHILOX) && !a.d2t &&
+        // warm L2 with the noise the merge will gather for this candidate (multistep rows
+        // draw their noise in ms_verify_kernel: their launch carries no noise pointer)
+        if (key && !MS && !cand_out && !(a.flags & SONIC_FLAG_PHILOX) && !a.d2t &&
             (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
           asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
       }
@@ -2664,6 +2665,134 @@ static int sm_count() {
   return n > 0 ? n : 148;
 }
 
+// ---------------------------------------------------------------------------------------
+// batched slot population (core/buffer.py:1026-1352: step_grammar, update, allocate)
+//
+// CTA (x, i) owns columns [x * POP_RANGE, +POP_RANGE) of call slot i's rows. The row parts
+// are built in shared memory (prompt histogram, bias row) or copied, and every destination
+// byte is written once with 16-byte stores where the row allows. A prompt of L tokens is
+// scanned by each of the slot's ceil(V / POP_RANGE) CTAs (from L2); every CTA counts only
+// its own columns, so no global atomics and no ordering between CTAs are needed.
+// ---------------------------------------------------------------------------------------
+
+constexpr int POP_RANGE = 4096;  // columns of one CTA
+constexpr int POP_NT = 256;
+
+// n int32 from shared memory (or zeros when src is NULL) to dst
+__device__ __forceinline__ void pop_store_i32(int32_t* dst, const int32_t* src, int n) {
+  int i0 = 0;
+  if (((uintptr_t)dst & 15) == 0) {
+    const int n4 = n >> 2;
+    for (int v = threadIdx.x; v < n4; v += POP_NT)
+      reinterpret_cast<int4*>(dst)[v] = src ? reinterpret_cast<const int4*>(src)[v] : make_int4(0, 0, 0, 0);
+    i0 = n4 << 2;
+  }
+  for (int e = i0 + threadIdx.x; e < n; e += POP_NT) dst[e] = src ? src[e] : 0;
+}
+
+// n int32 global to global
+__device__ __forceinline__ void pop_copy_i32(int32_t* dst, const int32_t* src, int n) {
+  int i0 = 0;
+  if ((((uintptr_t)dst | (uintptr_t)src) & 15) == 0) {
+    const int n4 = n >> 2;
+    for (int v = threadIdx.x; v < n4; v += POP_NT)
+      reinterpret_cast<int4*>(dst)[v] = __ldcs(reinterpret_cast<const int4*>(src) + v);
+    i0 = n4 << 2;
+  }
+  for (int e = i0 + threadIdx.x; e < n; e += POP_NT) dst[e] = __ldcs(src + e);
+}
+
+__global__ void __launch_bounds__(POP_NT) populate_kernel(const SonicPopulateArgs a) {
+  __shared__ __align__(16) int32_t hist[POP_RANGE];
+  __shared__ __align__(16) uint16_t brow[POP_RANGE];
+  const int tid = threadIdx.x;
+  const int i = blockIdx.y;
+  const int64_t slot = a.positions[i];
+  if (slot < 0 || slot >= a.num_slots) return;  // the host checks positions; never write outside
+  const int64_t V = a.vocab_size;
+  const int64_t c0 = (int64_t)blockIdx.x * POP_RANGE;
+  if (c0 >= V && blockIdx.x > 0) return;
+  const int n = (int)min((int64_t)POP_RANGE, V - c0);
+
+  if ((a.parts & SONIC_POPULATE_SCALARS) && blockIdx.x == 0 && tid < 10) {
+    // PinnedRelay.populate / RepetitionPenalties.populate / Flags.update + transfer
+    const uint16_t* f = a.values_bf16 + (int64_t)i * 6;
+    switch (tid) {
+      case 0: a.temperature[slot] = f[0]; break;
+      case 1: a.top_p[slot] = f[1]; break;
+      case 2: a.min_p[slot] = f[2]; break;
+      case 3: a.multiplicative[slot] = f[3]; break;
+      case 4: a.frequency[slot] = f[4]; break;
+      case 5: a.presence[slot] = f[5]; break;
+      case 6: a.top_k[slot] = a.values_i32[(int64_t)i * 2]; break;
+      case 7: a.top_logprobs[slot] = a.values_i32[(int64_t)i * 2 + 1]; break;
+      case 8: a.flags_target[slot] = a.indicators[(int64_t)i * 2]; break;
+      default: a.flags_draft[slot] = a.indicators[(int64_t)i * 2 + 1]; break;
+    }
+  }
+  if (n <= 0) return;
+
+  int32_t* ctx = a.context_counts + slot * a.counts_stride + c0;
+  int32_t* dec = a.decode_counts + slot * a.counts_stride + c0;
+  if (a.parts & SONIC_POPULATE_HISTOGRAM) {
+    // TokenCounts.populate + allocate: context = scatter_add of ones at the prompt's ids,
+    // decode = 0
+    for (int e = tid; e < POP_RANGE; e += POP_NT) hist[e] = 0;
+    __syncthreads();
+    const int64_t t0 = a.token_offsets[i], t1 = a.token_offsets[i + 1];
+    for (int64_t t = t0 + tid; t < t1; t += POP_NT) {
+      const int64_t tok = a.tokens[t];
+      if (tok >= c0 && tok < c0 + n) atomicAdd(&hist[tok - c0], 1);
+    }
+    __syncthreads();
+    pop_store_i32(ctx, hist, n);
+    pop_store_i32(dec, nullptr, n);
+  } else if (a.parts & SONIC_POPULATE_DENSE_COUNTS) {
+    // TokenCounts.update: both rows copied
+    pop_copy_i32(ctx, a.dense_context + (int64_t)i * V + c0, n);
+    pop_copy_i32(dec, a.dense_decode + (int64_t)i * V + c0, n);
+  }
+
+  if (a.parts & SONIC_POPULATE_BIAS) {
+    // PinnedRelay.update_bias + transfer: the row is zeroed, then the slot's entries land
+    for (int e = tid; e < POP_RANGE; e += POP_NT) brow[e] = 0;
+    __syncthreads();
+    if (a.bias_offsets) {
+      const int64_t b0 = a.bias_offsets[i], b1 = a.bias_offsets[i + 1];
+      for (int64_t t = b0 + tid; t < b1; t += POP_NT) {
+        const int64_t tok = a.bias_tokens[t];
+        if (tok >= c0 && tok < c0 + n) brow[tok - c0] = a.bias_values[t];
+      }
+    }
+    __syncthreads();
+    uint16_t* dst = a.bias + slot * a.bias_stride + c0;
+    int e0 = 0;
+    if (((uintptr_t)dst & 15) == 0) {
+      const int n8 = n >> 3;
+      for (int v = tid; v < n8; v += POP_NT) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(brow)[v];
+      e0 = n8 << 3;
+    }
+    for (int e = e0 + tid; e < n; e += POP_NT) dst[e] = brow[e];
+  }
+
+  if ((a.parts & SONIC_POPULATE_GRAMMAR) && a.grammar_rows[i] >= 0) {
+    // step_grammar: grammar[slot, step] (admission) or grammar[slot] (every step, one row
+    // broadcast or one row a step) = the bitmask
+    const int64_t W = (V + 31) / 32;
+    const int64_t w0 = c0 / 32;
+    const int nw = (int)min((int64_t)(POP_RANGE / 32), W - w0);
+    const int64_t src0 = a.grammar_rows[i];
+    const int nsrc = a.grammar_steps[i];
+    const int s0 = a.grammar_step >= 0 ? a.grammar_step : 0;
+    const int s1 = a.grammar_step >= 0 ? a.grammar_step + 1 : a.timesteps;
+    for (int s = s0; s < s1; ++s) {
+      const uint32_t* src = a.grammar_words + (src0 + (nsrc > 1 ? s - s0 : 0)) * W + w0;
+      uint32_t* dst = a.grammar + slot * a.grammar_slot_stride + (int64_t)s * a.grammar_step_stride + w0;
+      for (int e = tid; e < nw; e += POP_NT) dst[e] = src[e];
+    }
+  }
+}
+
 }  // namespace sonic
 
 extern "C" {
@@ -2714,6 +2843,49 @@ sonic_status sonic_indexed_copy(const void* source, void* target, int64_t rows, 
     e = cudaGetLastError();
   }
   return check_launch(e, "sonic_indexed_copy");
+}
+
+sonic_status sonic_populate_slots(const SonicPopulateArgs* a, void* stream) {
+  if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
+  if (a->count < 0) return fail(SONIC_ERR_INVALID_ARGUMENT, "count must be >= 0");
+  if (a->count == 0 || a->parts == 0) return SONIC_OK;
+  constexpr uint32_t all = SONIC_POPULATE_SCALARS | SONIC_POPULATE_HISTOGRAM | SONIC_POPULATE_DENSE_COUNTS |
+                           SONIC_POPULATE_BIAS | SONIC_POPULATE_GRAMMAR;
+  if (a->parts & ~all) return fail(SONIC_ERR_INVALID_ARGUMENT, "unknown SONIC_POPULATE_* bits");
+  if ((a->parts & SONIC_POPULATE_HISTOGRAM) && (a->parts & SONIC_POPULATE_DENSE_COUNTS))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "HISTOGRAM and DENSE_COUNTS are exclusive");
+  if (a->count > 65535) return fail(SONIC_ERR_INVALID_ARGUMENT, "count must be <= 65535");
+  if (a->num_slots <= 0 || a->vocab_size <= 0 || !a->positions)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "num_slots and vocab_size must be > 0 and positions non-NULL");
+  if ((a->parts & SONIC_POPULATE_SCALARS) &&
+      (!a->values_bf16 || !a->values_i32 || !a->indicators || !a->temperature || !a->top_p || !a->min_p ||
+       !a->top_k || !a->top_logprobs || !a->multiplicative || !a->frequency || !a->presence || !a->flags_target ||
+       !a->flags_draft))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "SCALARS needs every value and destination pointer");
+  const bool counts = (a->parts & (SONIC_POPULATE_HISTOGRAM | SONIC_POPULATE_DENSE_COUNTS)) != 0;
+  if (counts && (!a->context_counts || !a->decode_counts || a->counts_stride < a->vocab_size))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "count rows need both destinations and counts_stride >= vocab_size");
+  if ((a->parts & SONIC_POPULATE_HISTOGRAM) && (!a->token_offsets || !a->tokens))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "HISTOGRAM needs token_offsets and tokens");
+  if ((a->parts & SONIC_POPULATE_DENSE_COUNTS) && (!a->dense_context || !a->dense_decode))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "DENSE_COUNTS needs dense_context and dense_decode");
+  if ((a->parts & SONIC_POPULATE_BIAS) &&
+      (!a->bias || a->bias_stride < a->vocab_size || (a->bias_offsets && (!a->bias_tokens || !a->bias_values))))
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "BIAS needs the bias rows (bias_stride >= vocab_size) and its entries");
+  if (a->parts & SONIC_POPULATE_GRAMMAR) {
+    if (!a->grammar || !a->grammar_rows || !a->grammar_steps || !a->grammar_words || a->timesteps < 1)
+      return fail(SONIC_ERR_INVALID_ARGUMENT, "GRAMMAR needs the grammar buffer, its rows and timesteps >= 1");
+    if (a->grammar_step < -1 || a->grammar_step >= a->timesteps)
+      return fail(SONIC_ERR_INVALID_ARGUMENT, "grammar_step must be -1 or in [0, timesteps)");
+    const int64_t W = (a->vocab_size + 31) / 32;
+    if (a->grammar_step_stride < W || a->grammar_slot_stride < (int64_t)(a->timesteps - 1) * a->grammar_step_stride + W)
+      return fail(SONIC_ERR_INVALID_ARGUMENT, "grammar strides smaller than a row of ceil(vocab_size / 32) words");
+  }
+  const bool rows = counts || (a->parts & (SONIC_POPULATE_BIAS | SONIC_POPULATE_GRAMMAR));
+  const int64_t gx = rows ? (a->vocab_size + POP_RANGE - 1) / POP_RANGE : 1;
+  if (gx > 65535) return fail(SONIC_ERR_INVALID_ARGUMENT, "vocab_size too large");
+  populate_kernel<<<dim3((unsigned)gx, (unsigned)a->count), dim3(POP_NT), 0, (cudaStream_t)stream>>>(*a);
+  return check_launch(cudaGetLastError(), "sonic_populate_slots");
 }
 
 }  // extern "C"

@@ -309,7 +309,129 @@ def case_indexed_copy():
     save("indexed_copy", inputs, outputs, {"reference": "ops/copy.py:21-127 indexed_copy"})
 
 
+def _state(b) -> dict:
+    """The device-side fields of a reference SamplingBuffers, cloned."""
+    rep = b.repetition
+    w = b.weights
+    plain = lambda t: t.as_subclass(torch.Tensor).clone()  # noqa: E731
+    return {k: plain(v) for k, v in dict(
+        flags=b.flags.packed.clone(), temperature=b.temperature.clone(), top_p=b.top_p.clone(), min_p=b.min_p.clone(),
+        top_k=b.top_k.clone(), top_logprobs=b.top_logprobs.clone(), multiplicative=rep.multiplicative.clone(),
+        frequency=rep.frequency.clone(), presence=rep.presence.clone(), context=rep.counts.context.clone(),
+        decode=rep.counts.decode.clone(), bias=b.bias.clone(), grammar=b.grammar.view(torch.int32).clone(),
+        gumbel_target=torch.Tensor(w.gumbel.target).clone(), gumbel_draft=torch.Tensor(w.gumbel.draft).clone(),
+        uniform=torch.Tensor(w.uniform).clone(),
+    ).items()}
+
+
+def case_populate():
+    """The reference's own SamplingBuffers.allocate / update (core/buffer.py:1139-1352) on host
+    tensors: its pinned host mirrors become ordinary host tensors for this run (`pin_memory`
+    is dropped, there is no GPU here), and its pinned bias mirror starts zeroed. A sequence of
+    calls on one buffer per shape; the state after each call is saved.
+
+    Bitmasks are given only where `positions` is the identity prefix: the reference's
+    step_grammar indexes the bitmask list by slot id (core/buffer.py:1041-1049) while every
+    other list is aligned with `positions`, and the two readings agree only there."""
+    import sonic_sampler.ops.copy as ref_copy
+    from sonic_sampler.core.buffer import SamplingBuffers as RefBuffers
+
+    ref_copy.total_sm = lambda device: 148
+    originals = {n: getattr(torch, n) for n in ("empty", "empty_like", "tensor", "zeros")}
+
+    def nopin(fn):
+        def wrapped(*args, **kwargs):
+            kwargs.pop("pin_memory", None)
+            return fn(*args, **kwargs)
+        return wrapped
+
+    for n, f in originals.items():
+        setattr(torch, n, nopin(f))
+    try:
+        inputs, outputs = {}, {}
+        for tag, (B, T, V) in {"small": (6, 3, 1000), "ranges": (3, 2, 9000)}.items():
+            g = gen(41 + V)
+            W = (V + 31) // 32
+            torch.manual_seed(5 + V)
+            buf = RefBuffers.default(B, T, V, device=torch.device("cpu"))
+            buf.pinned.bias.zero_()
+            inputs[tag] = dict(shape=(B, T, V), initial=_state(buf), calls=[])
+            outputs[tag] = []
+
+            def params(n):
+                return dict(
+                    multiplicative=[float(x) for x in (torch.rand(n, generator=g) * 0.6 + 0.7)],
+                    frequency=[float(x) for x in (torch.rand(n, generator=g) - 0.5)],
+                    presence=[float(x) for x in (torch.rand(n, generator=g) * 0.4)],
+                    temperature=[float(x) for x in (torch.rand(n, generator=g) + 0.4)],
+                    top_k=[(128, 20, 1, 64)[int(i)] for i in torch.randint(0, 4, (n,), generator=g)],
+                    top_p=[float(x) for x in (torch.rand(n, generator=g) * 0.3 + 0.7)],
+                    min_p=[(0.0, 0.05)[int(i)] for i in torch.randint(0, 2, (n,), generator=g)],
+                    top_logprobs=[int(i) for i in torch.randint(0, 6, (n,), generator=g)],
+                )
+
+            def biases(n):
+                out = []
+                for j in range(n):
+                    if j % 3 == 1:
+                        out.append(None)
+                    else:
+                        toks = torch.randperm(V, generator=g)[: 2 + j % 4].tolist()
+                        out.append({t: float(torch.randn(1, generator=g)) * 2 for t in toks})
+                return out
+
+            def masks(n, full):
+                out = []
+                for j in range(n):
+                    if j % 2 == 1:
+                        out.append(None)
+                    else:
+                        rows = T if (full and j % 4 == 0) else 1
+                        m = torch.randint(-2**31, 2**31 - 1, (rows, W), generator=g, dtype=torch.int64).to(torch.int32)
+                        out.append(m[0] if rows == 1 else m)
+                return out
+
+            if tag == "small":
+                plan = [
+                    ("allocate", [4, 1, 3], False),
+                    ("allocate", [0, 1], True),
+                    ("update", [2, 0, 5], False),
+                    ("update", None, True),
+                ]
+            else:
+                plan = [("allocate", [2, 0], False), ("update", [0, 1, 2], True)]
+            for k, (kind, positions, grammar) in enumerate(plan):
+                n = len(positions) if positions else B
+                kw = params(n)
+                kw["biases"] = biases(n)
+                kw["greedy_drafts"] = [bool(j % 2) for j in range(n)]
+                if grammar:
+                    kw["bitmasks"] = masks(n, full=(kind == "update"))
+                if kind == "allocate":
+                    kw["encodings"] = [torch.randint(0, V, (int(torch.randint(0, 3 * V // 2, (1,), generator=g)),),
+                                                     generator=g) for _ in range(n)]
+                    kw["positions"] = positions
+                else:
+                    kw["counts"] = [(torch.randint(0, 9, (V,), generator=g, dtype=torch.int32),
+                                     torch.randint(0, 5, (V,), generator=g, dtype=torch.int32)) for _ in range(n)]
+                    kw["target_gumbel"] = [None] * n
+                    kw["positions"] = positions
+                seed = 1000 + 17 * k
+                inputs[tag]["calls"].append(dict(kind=kind, kwargs=kw, generator_seed=seed))
+                getattr(buf, kind)(generator=torch.Generator().manual_seed(seed), **kw)
+                outputs[tag].append(_state(buf))
+            if tag == "ranges":  # the larger shape keeps only its final noise
+                for snap in outputs[tag][:-1]:
+                    for key in ("gumbel_target", "gumbel_draft", "uniform"):
+                        snap.pop(key)
+    finally:
+        for n, f in originals.items():
+            setattr(torch, n, f)
+    save("populate", inputs, outputs, {"reference": "core/buffer.py:1139-1352 SamplingBuffers.update / allocate"})
+
+
 CASES = {
+    "populate": case_populate,
     "indexed_copy": case_indexed_copy,
     "topk_bf16": case_topk_bf16,
     "topk_bitonic": case_topk_bitonic,

@@ -51,7 +51,8 @@ def test_struct_layout_matches_header():
     """The ctypes mirror names every field of the header's structs in header order."""
     text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
     for cname, pyt in (("SonicSamplingParams", _abi.SamplingParams), ("SonicSingularArgs", _abi.SingularArgs),
-                       ("SonicMultistepArgs", _abi.MultistepArgs), ("SonicTopKArgs", _abi.TopKArgs)):
+                       ("SonicMultistepArgs", _abi.MultistepArgs), ("SonicTopKArgs", _abi.TopKArgs),
+                       ("SonicPopulateArgs", _abi.PopulateArgs)):
         body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
         fields = []
         for decl in body.split(";"):
@@ -116,3 +117,31 @@ def test_update_counts_without_decode_counts_message(lib):
     with pytest.raises(ValueError, match="`update_counts` is True but `decode_counts` is None"):
         prepare_singular(torch.zeros(2, 4096, dtype=torch.bfloat16), torch.zeros(2, dtype=torch.uint16),
                          update_counts=True)
+
+
+def test_populate_host_validation_without_gpu(lib):
+    """sonic_populate_slots rejects inconsistent arguments before launching."""
+    p = _abi.PopulateArgs()
+    assert _status(lib, "sonic_populate_slots", p)[0] == _abi.SONIC_OK  # nothing to do
+    p.count, p.parts = 2, _abi.POPULATE_HISTOGRAM | _abi.POPULATE_DENSE_COUNTS
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "exclusive" in msg
+    p.parts = 0x40
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "unknown" in msg
+    p.parts = _abi.POPULATE_SCALARS
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "positions" in msg
+    p.num_slots, p.vocab_size, p.positions = 4, 1000, 16
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "SCALARS" in msg
+    p.parts = _abi.POPULATE_GRAMMAR
+    p.grammar = p.grammar_rows = p.grammar_steps = p.grammar_words = 16
+    p.timesteps, p.grammar_step = 2, 2
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "grammar_step" in msg
+    p.grammar_step, p.grammar_step_stride, p.grammar_slot_stride = -1, 32, 40
+    st, msg = _status(lib, "sonic_populate_slots", p)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "strides" in msg
+    p.count = -1
+    assert _status(lib, "sonic_populate_slots", p)[0] == _abi.SONIC_ERR_INVALID_ARGUMENT
