@@ -14,6 +14,9 @@ the max over ranks.
 `--impl reference` times the CPU restatement of the reference algorithm (oracle/) on all
 host cores on a bounded sample of the same workload; it is the reference arm of the
 comparison and never touches the GPU.
+
+`--workload populate` measures the batched slot admission instead (SamplingBuffers.allocate
+through `sonic_populate_slots`; see run_populate).
 """
 
 from __future__ import annotations
