@@ -259,7 +259,7 @@ class SamplingBuffers:
             pop = self._population()
             batch = pop.new_batch(self._positions(positions, len(bitmasks)), self.bias.size(0), self.vocab_size)
             pop.pack_grammar(batch, bitmasks, self.grammar.size(1), timestep)
-            pop.launch_populate(self, batch, self._stager, stream)
+            self._launch(batch, None, batch.positions.tolist(), stream)
             if event is not None:
                 event.record(stream)
         return self
@@ -305,7 +305,8 @@ class SamplingBuffers:
     def _launch(self, batch, scoped, positions, stream) -> None:
         pop = self._population()
         pop.launch_populate(self, batch, self._stager, stream)
-        self.flags.update_host(scoped, positions)
+        if scoped is not None:
+            self.flags.update_host(scoped, positions)
 
     def update(self, counts, target_gumbel, multiplicative, frequency, presence, biases, temperature, top_k, top_p,
                min_p, top_logprobs, positions=None, indicators=None, greedy_drafts=False, prefill=False,

@@ -98,12 +98,28 @@ def indicator_tensor(values, device=None) -> torch.Tensor:
     return torch.tensor([int(v) for v in values], dtype=torch.uint16, device=device)
 
 
+_GREEDY = int(Indicator.GREEDY)
+
+
+def _indicator_bits(grammar, multiplicative, frequency, presence, logit_bias, temperature, top_k, top_p, min_p,
+                    top_k_logprobs, greedy_draft) -> int:
+    """Indicator.from_params as a plain int (the per-slot hot loop of a batch admission)."""
+    greedy = top_k == 1
+    bits = (bool(grammar) | (multiplicative != 1.0) << 1 | (frequency != 0.0) << 2 | (presence != 0.0) << 3
+            | bool(logit_bias) << 4 | (temperature != 1.0) << 5 | greedy << 6 | (1 < top_k < MAX_K) << 7)
+    if not greedy:
+        bits |= (0.0 < top_p < 1.0) << 8 | (0.0 < min_p < 1.0) << 9 | (0 < top_k_logprobs <= MAX_K) << 10
+        bits |= bool(greedy_draft) << 11
+    return int(bits)
+
+
 class ScopedIndicators:
     """Target and draft indicators of a list of slots (reference core/flags.py:229-432)."""
 
     def __init__(self, target: list, draft: list):
-        self.target = [Indicator(int(v)) for v in target]
-        self.draft = [Indicator(int(v)) for v in draft]
+        # plain ints with the Indicator bit values (Indicator is an int subclass)
+        self.target = [int(v) for v in target]
+        self.draft = [int(v) for v in draft]
 
     @classmethod
     def from_pairs(cls, pairs) -> "ScopedIndicators":
@@ -134,21 +150,24 @@ class ScopedIndicators:
             top_logprobs or fill(0),
             drafter,
         )
-        target = [Indicator.from_params(*r) for r in rows]
-        draft = [t.greedy() if g else t.disable(Indicator.TOP_K_LOGPROBS) for g, t in zip(drafter, target)]
+        target = [_indicator_bits(*r) for r in rows]
+        greedy_mask = int(Indicator.all() ^ Indicator.stochastic() ^ Indicator.TOP_K_LOGPROBS
+                          ^ Indicator.STOCHASTIC_VERIFY_GREEDY_DRAFT)
+        no_top_z = int(Indicator.all() ^ Indicator.TOP_K_LOGPROBS)
+        draft = [((t & greedy_mask) | int(Indicator.GREEDY)) if g else (t & no_top_z) for g, t in zip(drafter, target)]
         return cls(target, draft)
 
     @property
     def has_stochastic_target(self) -> bool:
-        return any(not (v & Indicator.GREEDY) for v in self.target)
+        return any(not (v & _GREEDY) for v in self.target)
 
     @property
     def has_stochastic_draft(self) -> bool:
-        return any(not (v & Indicator.GREEDY) for v in self.draft)
+        return any(not (v & _GREEDY) for v in self.draft)
 
     @property
     def stochastic_selectors(self) -> list[tuple[bool, bool]]:
-        return [(not (t & Indicator.GREEDY), not (d & Indicator.GREEDY)) for t, d in zip(self.target, self.draft)]
+        return [(not (t & _GREEDY), not (d & _GREEDY)) for t, d in zip(self.target, self.draft)]
 
     def subset(self, indices) -> "ScopedIndicators":
         return ScopedIndicators([self.target[i] for i in indices], [self.draft[i] for i in indices])

@@ -112,15 +112,14 @@ def pack_histogram(batch: SlotBatch, encodings: Sequence[Tensor]) -> None:
     if len(encodings) != batch.count:
         raise ValueError("encodings must have one entry per position")
     V = batch.vocab_size
-    arrays = []
-    for e in encodings:
-        a = (e.detach().cpu().numpy() if isinstance(e, Tensor) else np.asarray(e)).reshape(-1).astype(np.int64)
-        if a.size and (a.min() < 0 or a.max() >= V):
-            raise RuntimeError(f"token id out of bounds for a vocabulary of {V}")
-        arrays.append(a)
-    lengths = np.asarray([a.size for a in arrays], dtype=np.int64)
+    flat = [e.detach().reshape(-1).cpu() if isinstance(e, Tensor) else torch.as_tensor(np.asarray(e)).reshape(-1)
+            for e in encodings]
+    lengths = np.fromiter((t.numel() for t in flat), dtype=np.int64, count=len(flat))
+    ids = torch.cat(flat).to(torch.int64) if flat else torch.zeros(0, dtype=torch.int64)
+    if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= V):
+        raise RuntimeError(f"token id out of bounds for a vocabulary of {V}")
     batch.token_offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
-    batch.tokens = (np.concatenate(arrays) if arrays else np.zeros(0, np.int64)).astype(np.int32)
+    batch.tokens = ids.to(torch.int32).numpy()
     batch.parts |= HISTOGRAM
 
 
@@ -154,17 +153,16 @@ def pack_bias(batch: SlotBatch, biases: Sequence[dict[int, float] | None] | None
     biases = list(biases) if biases else [None] * n
     if len(biases) != n:
         raise ValueError("biases must have one entry per position")
-    toks, vals, lengths = [], [], []
-    for mapping in biases:
-        items = list(mapping.items()) if mapping else []
-        for t, _ in items:
-            if not 0 <= int(t) < V:
-                raise ValueError(f"logit bias token {t} outside the vocabulary of {V}")
-        toks += [int(t) for t, _ in items]
-        vals += [float(v) for _, v in items]
-        lengths.append(len(items))
+    maps = [m if m else {} for m in biases]
+    lengths = np.fromiter((len(m) for m in maps), dtype=np.int64, count=n)
+    total = int(lengths.sum())
+    toks = np.fromiter((t for m in maps for t in m.keys()), dtype=np.int64, count=total)
+    vals = [float(v) for m in maps for v in m.values()]
+    if total and (toks.min() < 0 or toks.max() >= V):
+        bad = toks[(toks < 0) | (toks >= V)][0]
+        raise ValueError(f"logit bias token {bad} outside the vocabulary of {V}")
     batch.bias_offsets = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
-    batch.bias_tokens = np.asarray(toks, dtype=np.int32)
+    batch.bias_tokens = toks.astype(np.int32)
     batch.bias_values = bf16_bits(vals)
     batch.parts |= BIAS
 
@@ -179,27 +177,26 @@ def pack_grammar(batch: SlotBatch, bitmasks: Sequence[Tensor | None] | None, tim
     if len(bitmasks) != batch.count:
         raise ValueError("bitmasks must have one entry per position")
     W = (batch.vocab_size + 31) // 32
-    rows, nsteps, words = [], [], []
+    rows, nsteps, blocks = [], [], []
     next_row = 0
     for m in bitmasks:
         if m is None:
             rows.append(-1)
             nsteps.append(0)
             continue
-        a = (m.detach().cpu() if isinstance(m, Tensor) else torch.as_tensor(m)).contiguous()
-        if a.element_size() != 4:
+        t = m if isinstance(m, Tensor) else torch.as_tensor(np.asarray(m))
+        if t.element_size() != 4:
             raise ValueError("grammar bitmasks are 32-bit words")
-        a = a.view(torch.int32).numpy().view(np.uint32)
-        a = a.reshape(-1, a.shape[-1]) if a.ndim > 1 else a.reshape(1, -1)
-        if a.shape[-1] != W or (a.shape[0] != 1 and (step is not None or a.shape[0] != timesteps)):
+        t = t.detach().reshape(-1, t.shape[-1]) if t.dim() > 1 else t.detach().reshape(1, -1)
+        if t.shape[-1] != W or (t.shape[0] != 1 and (step is not None or t.shape[0] != timesteps)):
             raise ValueError(f"a bitmask must have shape [{W}]" + ("" if step is not None else f" or [{timesteps}, {W}]"))
         rows.append(next_row)
-        nsteps.append(a.shape[0])
-        words.append(a)
-        next_row += a.shape[0]
+        nsteps.append(t.shape[0])
+        blocks.append(t.view(torch.int32) if t.dtype != torch.int32 else t)
+        next_row += t.shape[0]
     batch.grammar_rows = np.asarray(rows, dtype=np.int32)
     batch.grammar_steps = np.asarray(nsteps, dtype=np.int32)
-    batch.grammar_words = np.concatenate(words).astype(np.uint32)
+    batch.grammar_words = torch.cat(blocks).cpu().numpy().view(np.uint32)
     batch.grammar_step = -1 if step is None else int(step)
     batch.parts |= GRAMMAR
 

@@ -1009,85 +1009,6 @@ __device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r
 }
 
 // ---------------------------------------------------------------------------------------
-// units of a streaming launch: a unit is one split (<= 65536 columns) of one row, in
-// row-major order; a CTA looks its units up in a shared-memory table
-// ---------------------------------------------------------------------------------------
-
-constexpr int MAX_CTA_UNITS = 128;  // units one CTA streams at most
-
-enum StreamBits : uint32_t { kSgG = 1, kSgDec = 2, kSgCtx = 4, kSgBias = 8 };
-
-struct UnitTable {
-  int32_t r[MAX_CTA_UNITS];        // row
-  int32_t slot[MAX_CTA_UNITS];     // slot; -1: the unit is skipped
-  int32_t gslot[MAX_CTA_UNITS];    // grammar row
-  int32_t margin[MAX_CTA_UNITS];   // multistep: first row of the request
-  int16_t split[MAX_CTA_UNITS];
-  uint8_t step[MAX_CTA_UNITS];     // multistep: step of the row
-  uint8_t sg[MAX_CTA_UNITS];       // StreamBits of the row
-  int32_t cum[MAX_CTA_UNITS + 1];  // full ring chunks of the units before
-};
-
-__device__ __forceinline__ uint32_t stream_bits(const Needs& n) {
-  return (n.g ? kSgG : 0u) | (n.dec ? kSgDec : 0u) | (n.ctx ? kSgCtx : 0u) | (n.bias ? kSgBias : 0u);
-}
-
-// Block-wide: fills the table for units [u0, u0 + nu) and returns the union of their
-// StreamBits. `chunk` = columns of a ring chunk (0: no ring).
-template <bool MS>
-__device__ uint32_t build_unit_table(UnitTable& ut, const SonicSingularArgs& a, const MsRows& ms, int64_t u0, int nu,
-                                     int splits, int cols, int chunk, int* scan) {
-  const SonicSamplingParams& P = a.params;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  uint32_t bits = 0;
-  int nch = 0;
-  if (tid < nu) {
-    const int64_t u = u0 + tid;
-    const int64_t r = u / splits;
-    const int split = (int)(u % splits);
-    int64_t req = r, margin = 0;
-    int step = 0;
-    bool ok = !MS || ms_row(ms, r, req, step, margin);
-    int64_t slot = ok ? load_slot(P, req) : -1;
-    if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
-      ok = false;
-      slot = -1;
-    }
-    ut.r[tid] = (int32_t)r;
-    ut.slot[tid] = (int32_t)slot;
-    ut.gslot[tid] = (int32_t)(MS ? slot * (ms.lookahead + 1) + step : slot);
-    ut.margin[tid] = (int32_t)margin;
-    ut.split[tid] = (int16_t)split;
-    ut.step[tid] = (uint8_t)step;
-    if (ok) {
-      bits = stream_bits(row_consts(P, slot, P.indicators[slot]).nd);
-      const int64_t c0 = (int64_t)split * cols;
-      const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
-      nch = chunk ? (int)((c1 - c0) / chunk) : 0;
-    }
-    ut.sg[tid] = (uint8_t)bits;
-  }
-  // exclusive prefix of the chunk counts (nu <= MAX_CTA_UNITS = 4 warps of lanes)
-  int incl = nch;
-#pragma unroll
-  for (int d = 1; d < 32; d <<= 1) {
-    const int o = __shfl_up_sync(kFull, incl, d);
-    if (lane >= d) incl += o;
-  }
-  if (lane == 31 && warp < MAX_CTA_UNITS / 32) scan[warp] = incl;
-  __syncthreads();
-  if (tid < nu) {
-    int off = 0;
-    for (int w = 0; w < warp; ++w) off += scan[w];
-    ut.cum[tid] = off + incl - nch;
-    if (tid == nu - 1) ut.cum[nu] = off + incl;
-  }
-  // __syncthreads_or only says whether any thread's value is nonzero: one call per bit
-  return (__syncthreads_or((int)(bits & kSgG)) ? kSgG : 0u) | (__syncthreads_or((int)(bits & kSgDec)) ? kSgDec : 0u) |
-         (__syncthreads_or((int)(bits & kSgCtx)) ? kSgCtx : 0u) | (__syncthreads_or((int)(bits & kSgBias)) ? kSgBias : 0u);
-}
-
-// ---------------------------------------------------------------------------------------
 // fused singular: prologue + top-128 per split + merge + selection
 // (ops/prologue.py:272 + ops/singular.py:154)
 // ---------------------------------------------------------------------------------------
@@ -1096,13 +1017,10 @@ template <int MODE, bool INDIRECT, bool MS>
 __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, uint64_t* cand_out, const MsRows ms) {
   __shared__ __align__(16) RowSmem<uint32_t> st;
-  __shared__ UnitTable ut;
-  __shared__ int scan[MAX_CTA_UNITS / 32];
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // one CTA per (row, split) unit, row-major
-  const int split = (int)(blockIdx.x % (unsigned)splits);
-  const int64_t r = blockIdx.x / (unsigned)splits;
+  const int split = blockIdx.x;
+  const int64_t r = blockIdx.y;
   const SonicSamplingParams& P = a.params;
   const int64_t c0 = (int64_t)split * cols;
   const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
@@ -1131,13 +1049,15 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   };
 
   // MS: row r is step `step` of multistep request `req` (rows [margin, margin + T))
-  const uint32_t sgu = build_unit_table<MS>(ut, a, ms, (int64_t)blockIdx.x, 1, splits, cols, MODE == kTma ? CH : 0, scan);
-  const int64_t slot = ut.slot[0];
-  const int64_t margin = ut.margin[0];
-  const int step = ut.step[0];
-  if (slot < 0) {
-    // a row outside every request, or an out-of-range slot id: no CTA of this row touches
-    // per-slot buffers or the ticket
+  int64_t req = r, margin = 0;
+  int step = 0;
+  if (MS && !ms_row(ms, r, req, step, margin)) {
+    drain();
+    return;
+  }
+  const int64_t slot = load_slot(P, req);
+  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
+    // out-of-range slot id: no CTA of this row touches per-slot buffers or the ticket
     if (!MS && split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
     drain();
     return;
@@ -1153,43 +1073,36 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const int ntok = !rc.nd.dec ? 0 : (MS ? step : (a.drafted_tokens ? a.lookahead : 0));
   if (tid < ntok) st.toks[tid] = MS ? ms.tokens[margin + tid] : a.drafted_tokens[slot * a.drafted_stride + tid];
   // grammar row: per slot, or per (slot, step) in multistep (ops/prologue.py:29-54)
-  const int64_t gslot = ut.gslot[0];
+  const int64_t gslot = MS ? slot * (ms.lookahead + 1) + step : slot;
   // streams of the bulk-copy ring (see below)
   const int64_t shard = a.shard_offset;
   const uint32_t* grow = rc.nd.g ? P.grammar + gslot * P.grammar_stride : nullptr;
   const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
   const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
   const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
-  // stage layout: the streams the CTA's units read, as many stages as fit the ring
+  // stage layout of this row: only the streams it reads, as many stages as fit the ring
   const int sg_d = CH * 2;
-  const int sg_c = sg_d + ((sgu & kSgDec) ? CH * 4 : 0);
-  const int sg_b = sg_c + ((sgu & kSgCtx) ? CH * 4 : 0);
-  const int sg_g = sg_b + ((sgu & kSgBias) ? CH * 2 : 0);
-  const int sg_stage = sg_g + ((sgu & kSgG) ? CH / 8 : 0);  // a multiple of 256 bytes
+  const int sg_c = sg_d + (drow ? CH * 4 : 0);
+  const int sg_b = sg_c + (crow ? CH * 4 : 0);
+  const int sg_g = sg_b + (brow ? CH * 2 : 0);
+  const int sg_stage = sg_g + (grow ? CH / 8 : 0);  // = the bytes of one chunk (multiple of 256)
   const int nst = min(MAX_RING_STAGES, RING_BYTES / sg_stage);
-  // ring chunk q of the CTA (its unit found in the table) into `stage`; one thread
-  auto issue_chunk = [&](int q, int stage) {
-    int i = 0;
-    while (q >= ut.cum[i + 1]) ++i;
-    const uint32_t b = ut.sg[i];
-    const int64_t cc = (int64_t)ut.split[i] * cols + (int64_t)(q - ut.cum[i]) * CH;
-    const int64_t us = ut.slot[i];
+  auto issue_chunk = [&](int i, int stage) {  // one thread
     unsigned char* sp = smem_ring + stage * sg_stage;
     uint64_t* bar = &st.bars[stage];
-    const uint32_t aux = ((b & kSgDec) ? CH * 4 : 0) + ((b & kSgCtx) ? CH * 4 : 0) + ((b & kSgBias) ? CH * 2 : 0) +
-                         ((b & kSgG) ? CH / 8 : 0);
-    if (q == 0) {
+    const int64_t cc = c0 + (int64_t)i * CH;
+    if (i == 0) {
       // the logits are on their way already
-      if (aux) mbar_expect_tx(bar, aux);
+      if (sg_stage > CH * 2) mbar_expect_tx(bar, (uint32_t)(sg_stage - CH * 2));
       else mbar_arrive(bar);
     } else {
-      mbar_expect_tx(bar, (uint32_t)(CH * 2) + aux);
-      bulk_load(sp, (const uint16_t*)a.logits + (int64_t)ut.r[i] * a.logits_stride + cc, CH * 2, bar);
+      mbar_expect_tx(bar, (uint32_t)sg_stage);
+      bulk_load(sp, xrow + cc, CH * 2, bar);
     }
-    if (b & kSgDec) bulk_load(sp + sg_d, P.decode_counts + us * P.counts_stride + cc + shard, CH * 4, bar);
-    if (b & kSgCtx) bulk_load(sp + sg_c, P.context_counts + us * P.counts_stride + cc + shard, CH * 4, bar);
-    if (b & kSgBias) bulk_load(sp + sg_b, P.bias + us * P.bias_stride + cc + shard, CH * 2, bar);
-    if (b & kSgG) bulk_load(sp + sg_g, P.grammar + (int64_t)ut.gslot[i] * P.grammar_stride + (cc + shard) / 32, CH / 8, bar);
+    if (drow) bulk_load(sp + sg_d, drow + cc + shard, CH * 4, bar);
+    if (crow) bulk_load(sp + sg_c, crow + cc + shard, CH * 4, bar);
+    if (brow) bulk_load(sp + sg_b, brow + cc + shard, CH * 2, bar);
+    if (grow) bulk_load(sp + sg_g, grow + (cc + shard) / 32, CH / 8, bar);
   };
   if (tid == 0) {
     st.best = 0ull;
@@ -2407,7 +2320,7 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
   if (mode == kVec && !ind && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
-  dim3 grid((unsigned)(p.splits * a->rows));
+  dim3 grid(p.splits, a->rows);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
@@ -2541,7 +2454,7 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
-  const dim3 grid((unsigned)(p.splits * rows));
+  const dim3 grid(p.splits, (unsigned)rows);
   cudaError_t e;
   if (mode == kTma)
     e = launch(singular_kernel<kTma, false, true>, grid, (size_t)RING_BYTES, st, pdl, sa, p.splits, p.cols, l2, ws,

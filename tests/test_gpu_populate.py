@@ -142,3 +142,30 @@ def test_gpu_population_unaligned_rows():
         assert torch.equal(bits(got[name]), bits(want[name])), name
     on = (got["flags"][:, 0].to(torch.int32) & BIAS_BIT) != 0
     assert on.any()
+
+
+def test_gpu_step_weights_stages_draft_noise():
+    """step_weights (core/buffer.py:1054-1096): the draft noise of slots whose draft indicator is
+    stochastic moves into their target noise, then the stochastic slots' noise is refreshed
+    (the draft rows of stochastically drafted slots, the target rows otherwise)."""
+    B, T, V = 6, 3, 4096
+    buf = SamplingBuffers.default(B, T, V, device=DEV)
+    g = torch.Generator().manual_seed(11)
+    kw = random_params(4, g, V)
+    kw["top_k"] = [1, 30, 30, 30]  # slot 0 greedy
+    buf.allocate([torch.randint(0, V, (100,), generator=g) for _ in range(4)], positions=[0, 2, 3, 5],
+                 greedy_drafts=[False, False, True, False], **kw)
+    torch.cuda.synchronize()
+    before_t = buf.weights.gumbel.target.clone()
+    before_d = buf.weights.gumbel.draft.clone()
+    positions = [0, 2, 3, 5]
+    buf.step_weights(positions, indices=torch.tensor(positions, device=DEV), generator=torch.Generator(DEV).manual_seed(5))
+    torch.cuda.synchronize()
+    t, d = buf.weights.gumbel.target, buf.weights.gumbel.draft
+    # slot 2: stochastic draft -> target = old draft, draft refreshed
+    assert torch.equal(t[2], before_d[2]) and not torch.equal(d[2], before_d[2])
+    # slot 3: greedy draft -> no staging; target refreshed, draft untouched
+    assert not torch.equal(t[3], before_t[3]) and torch.equal(d[3], before_d[3])
+    # slot 0: greedy target -> untouched; slots 1 and 4 not in the call -> untouched
+    for s in (0, 1, 4):
+        assert torch.equal(t[s], before_t[s]) and torch.equal(d[s], before_d[s])

@@ -58,7 +58,8 @@ def with_oracle_launch(buf: SamplingBuffers) -> SamplingBuffers:
 
     def launch(batch, scoped, positions, stream):
         oracle.populate_slots(batch, dest)
-        buf.flags.update_host(scoped, positions)
+        if scoped is not None:
+            buf.flags.update_host(scoped, positions)
 
     buf._launch = launch
     return buf
@@ -159,3 +160,18 @@ def test_population_needs_cuda_buffers():
     buf = SamplingBuffers.default(2, 1, 64)
     with pytest.raises(ValueError, match="CUDA"):
         buf.allocate([torch.tensor([1])], [1.0], [0.0], [0.0], [None], [1.0], [128], [1.0], [0.0], [0], [0])
+
+
+def test_indicator_bits_match_indicator_from_params():
+    """The batch path's integer resolution equals Indicator.from_params (core/flags.py:150-184)."""
+    import random
+
+    from sonic_sampler_b200.core.flags import _indicator_bits
+
+    rng = random.Random(1)
+    for _ in range(5000):
+        args = (rng.random() < .5, rng.choice([1.0, 0.9, 1.2]), rng.choice([0.0, 0.3]), rng.choice([0.0, -0.1]),
+                rng.random() < .5, rng.choice([1.0, 0.0, 0.7]), rng.choice([1, 2, 20, 127, 128]),
+                rng.choice([1.0, 0.0, 0.9, 1.5]), rng.choice([0.0, 0.05, 1.0]), rng.choice([0, 3, 128, 129]),
+                rng.random() < .5)
+        assert _indicator_bits(*args) == int(Indicator.from_params(*args)), args
