@@ -2590,6 +2590,7 @@ static int sm_count() {
 
 constexpr int POP_RANGE = 4096;  // columns of one CTA
 constexpr int POP_NT = 256;
+constexpr int POP_UNROLL = 8;  // prompt ids a thread loads before counting them
 
 // n int32 from shared memory (or zeros when src is NULL) to dst
 __device__ __forceinline__ void pop_store_i32(int32_t* dst, const int32_t* src, int n) {
@@ -2620,12 +2621,32 @@ __global__ void __launch_bounds__(POP_NT) populate_kernel(const SonicPopulateArg
   __shared__ __align__(16) uint16_t brow[POP_RANGE];
   const int tid = threadIdx.x;
   const int i = blockIdx.y;
-  const int64_t slot = a.positions[i];
-  if (slot < 0 || slot >= a.num_slots) return;  // the host checks positions; never write outside
   const int64_t V = a.vocab_size;
   const int64_t c0 = (int64_t)blockIdx.x * POP_RANGE;
-  if (c0 >= V && blockIdx.x > 0) return;
-  const int n = (int)min((int64_t)POP_RANGE, V - c0);
+  const int n = (int)min((int64_t)POP_RANGE, V - c0);  // > 0: the grid covers V exactly
+  const bool hist_on = (a.parts & SONIC_POPULATE_HISTOGRAM) != 0;
+  const bool dense_on = !hist_on && (a.parts & SONIC_POPULATE_DENSE_COUNTS) != 0;
+  const bool bias_on = (a.parts & SONIC_POPULATE_BIAS) != 0;
+  const bool gram_on = (a.parts & SONIC_POPULATE_GRAMMAR) != 0;
+
+  // first round trip: every per-slot offset, loaded together
+  const int64_t slot = a.positions[i];
+  int64_t t0 = 0, t1 = 0, b0 = 0, b1 = 0;
+  int64_t grow = -1;
+  int gsteps = 0;
+  if (hist_on) {
+    t0 = a.token_offsets[i];
+    t1 = a.token_offsets[i + 1];
+  }
+  if (bias_on && a.bias_offsets) {
+    b0 = a.bias_offsets[i];
+    b1 = a.bias_offsets[i + 1];
+  }
+  if (gram_on) {
+    grow = a.grammar_rows[i];
+    gsteps = a.grammar_steps[i];
+  }
+  if (slot < 0 || slot >= a.num_slots) return;  // the host checks positions; never write outside
 
   if ((a.parts & SONIC_POPULATE_SCALARS) && blockIdx.x == 0 && tid < 10) {
     // PinnedRelay.populate / RepetitionPenalties.populate / Flags.update + transfer
@@ -2643,65 +2664,90 @@ __global__ void __launch_bounds__(POP_NT) populate_kernel(const SonicPopulateArg
       default: a.flags_draft[slot] = a.indicators[(int64_t)i * 2 + 1]; break;
     }
   }
-  if (n <= 0) return;
 
   int32_t* ctx = a.context_counts + slot * a.counts_stride + c0;
   int32_t* dec = a.decode_counts + slot * a.counts_stride + c0;
-  if (a.parts & SONIC_POPULATE_HISTOGRAM) {
-    // TokenCounts.populate + allocate: context = scatter_add of ones at the prompt's ids,
-    // decode = 0
-    for (int e = tid; e < POP_RANGE; e += POP_NT) hist[e] = 0;
-    __syncthreads();
-    const int64_t t0 = a.token_offsets[i], t1 = a.token_offsets[i + 1];
-    for (int64_t t = t0 + tid; t < t1; t += POP_NT) {
-      const int64_t tok = a.tokens[t];
-      if (tok >= c0 && tok < c0 + n) atomicAdd(&hist[tok - c0], 1);
-    }
-    __syncthreads();
-    pop_store_i32(ctx, hist, n);
-    pop_store_i32(dec, nullptr, n);
-  } else if (a.parts & SONIC_POPULATE_DENSE_COUNTS) {
+  if (hist_on) {
+    pop_store_i32(dec, nullptr, n);  // TokenCounts.allocate: decode = 0, no dependency
+  } else if (dense_on) {
     // TokenCounts.update: both rows copied
     pop_copy_i32(ctx, a.dense_context + (int64_t)i * V + c0, n);
     pop_copy_i32(dec, a.dense_decode + (int64_t)i * V + c0, n);
   }
 
-  if (a.parts & SONIC_POPULATE_BIAS) {
-    // PinnedRelay.update_bias + transfer: the row is zeroed, then the slot's entries land
-    for (int e = tid; e < POP_RANGE; e += POP_NT) brow[e] = 0;
+  // second round trip: the first prompt ids, bias entry and bitmask word of this thread,
+  // issued together before the shared-memory rows are zeroed
+  int32_t tk[POP_UNROLL];
+#pragma unroll
+  for (int k = 0; k < POP_UNROLL; ++k) {
+    const int64_t t = t0 + k * POP_NT + tid;
+    tk[k] = t < t1 ? __ldg(a.tokens + t) : -1;
+  }
+  int32_t btok = -1;
+  uint16_t bval = 0;
+  if (b0 + tid < b1) {
+    btok = __ldg(a.bias_tokens + b0 + tid);
+    bval = __ldg(a.bias_values + b0 + tid);
+  }
+  const int64_t W = (V + 31) / 32;
+  const int64_t w0 = c0 / 32;
+  const int nw = (int)min((int64_t)(POP_RANGE / 32), W - w0);
+  uint32_t gword = 0;
+  if (grow >= 0 && tid < nw) gword = __ldg(a.grammar_words + grow * W + w0 + tid);
+
+  if (hist_on || bias_on) {
+    if (hist_on)
+      for (int e = tid; e < POP_RANGE / 4; e += POP_NT) reinterpret_cast<int4*>(hist)[e] = make_int4(0, 0, 0, 0);
+    if (bias_on)
+      for (int e = tid; e < POP_RANGE / 8; e += POP_NT) reinterpret_cast<uint4*>(brow)[e] = make_uint4(0, 0, 0, 0);
     __syncthreads();
-    if (a.bias_offsets) {
-      const int64_t b0 = a.bias_offsets[i], b1 = a.bias_offsets[i + 1];
-      for (int64_t t = b0 + tid; t < b1; t += POP_NT) {
+    if (hist_on) {
+      // TokenCounts.populate: scatter_add of ones at the prompt's ids in this CTA's columns,
+      // POP_UNROLL independent loads a thread ahead of their shared-memory atomics
+      for (int64_t base = t0;;) {
+#pragma unroll
+        for (int k = 0; k < POP_UNROLL; ++k)
+          if (tk[k] >= c0 && tk[k] < c0 + n) atomicAdd(&hist[tk[k] - c0], 1);
+        base += (int64_t)POP_NT * POP_UNROLL;
+        if (base >= t1) break;
+#pragma unroll
+        for (int k = 0; k < POP_UNROLL; ++k) {
+          const int64_t t = base + k * POP_NT + tid;
+          tk[k] = t < t1 ? __ldg(a.tokens + t) : -1;
+        }
+      }
+    }
+    if (bias_on) {
+      // PinnedRelay.update_bias: the slot's entries land on the zeroed row
+      if (btok >= c0 && btok < c0 + n) brow[btok - c0] = bval;
+      for (int64_t t = b0 + POP_NT + tid; t < b1; t += POP_NT) {
         const int64_t tok = a.bias_tokens[t];
         if (tok >= c0 && tok < c0 + n) brow[tok - c0] = a.bias_values[t];
       }
     }
     __syncthreads();
-    uint16_t* dst = a.bias + slot * a.bias_stride + c0;
-    int e0 = 0;
-    if (((uintptr_t)dst & 15) == 0) {
-      const int n8 = n >> 3;
-      for (int v = tid; v < n8; v += POP_NT) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(brow)[v];
-      e0 = n8 << 3;
+    if (hist_on) pop_store_i32(ctx, hist, n);
+    if (bias_on) {
+      uint16_t* dst = a.bias + slot * a.bias_stride + c0;
+      int e0 = 0;
+      if (((uintptr_t)dst & 15) == 0) {
+        const int n8 = n >> 3;
+        for (int v = tid; v < n8; v += POP_NT) reinterpret_cast<uint4*>(dst)[v] = reinterpret_cast<const uint4*>(brow)[v];
+        e0 = n8 << 3;
+      }
+      for (int e = e0 + tid; e < n; e += POP_NT) dst[e] = brow[e];
     }
-    for (int e = e0 + tid; e < n; e += POP_NT) dst[e] = brow[e];
   }
 
-  if ((a.parts & SONIC_POPULATE_GRAMMAR) && a.grammar_rows[i] >= 0) {
+  if (grow >= 0 && tid < nw) {
     // step_grammar: grammar[slot, step] (admission) or grammar[slot] (every step, one row
     // broadcast or one row a step) = the bitmask
-    const int64_t W = (V + 31) / 32;
-    const int64_t w0 = c0 / 32;
-    const int nw = (int)min((int64_t)(POP_RANGE / 32), W - w0);
-    const int64_t src0 = a.grammar_rows[i];
-    const int nsrc = a.grammar_steps[i];
     const int s0 = a.grammar_step >= 0 ? a.grammar_step : 0;
     const int s1 = a.grammar_step >= 0 ? a.grammar_step + 1 : a.timesteps;
+    uint32_t* dst = a.grammar + slot * a.grammar_slot_stride + w0 + tid;
     for (int s = s0; s < s1; ++s) {
-      const uint32_t* src = a.grammar_words + (src0 + (nsrc > 1 ? s - s0 : 0)) * W + w0;
-      uint32_t* dst = a.grammar + slot * a.grammar_slot_stride + (int64_t)s * a.grammar_step_stride + w0;
-      for (int e = tid; e < nw; e += POP_NT) dst[e] = src[e];
+      const uint32_t w = (gsteps > 1 && s > s0) ? __ldg(a.grammar_words + (grow + (s - s0)) * W + w0 + tid) : gword;
+      dst[(int64_t)s * a.grammar_step_stride] = w;
     }
   }
 }
