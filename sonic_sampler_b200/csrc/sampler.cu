@@ -1116,6 +1116,13 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   WarpTopK<uint32_t> w;
   wtk_init(w, st.lists[warp], kFiniteFloor, lane);  // the first wtk_adopt takes the fast-path pair from st.cut
   uint64_t best = 0;
+  // Greedy rows whose only processor is a temperature t in (0, max]: bf16(x / t) is monotone
+  // in the logit x, so a column whose logit is below the warp's floor (the smallest bf16
+  // whose tempered value reaches the best key the warp has seen) has a strictly smaller key
+  // and is skipped with one compare; the others are tempered and keyed exactly.
+  const bool gskip = greedy && !rc.nd.proc && rc.nd.temp && rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f;
+  float gfloor = __int_as_float(0xff800000);
+  uint64_t gbest = 0;  // the warp's best key when gfloor was set
   bool tq = rc.fast && rc.nd.temp;  // fast-path queues hold pre-temperature keys
   auto final_of = [&](float v) { return final_value(v, rc); };
 
@@ -1129,6 +1136,36 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   // exact path: every processor on every column, then the candidate test
   auto exact_group = [&](Raw8& raw, int64_t c, int nvalid) {
+    if (gskip) {
+      bool rose = false;
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        const float lo = bf2_lo(raw.x[p]), hi = bf2_hi(raw.x[p]);
+        const bool e0 = 2 * p < nvalid && !(lo < gfloor);
+        const bool e1 = 2 * p + 1 < nvalid && !(hi < gfloor);
+        if (e0 || e1) {
+          // the temperature step of process_pair, on this pair only
+          const uint32_t tp = rc.temp_fast ? bf2_pack(__fmul_rn(lo, rc.rtemp), __fmul_rn(hi, rc.rtemp))
+                                           : bf2_pack(__fdiv_rn(lo, rc.temp), __fdiv_rn(hi, rc.temp));
+          const uint64_t k0 = e0 ? greedy_key_bits(tp & 0xffffu, c + 2 * p, log2bn) : 0ull;
+          const uint64_t k1 = e1 ? greedy_key_bits(tp >> 16, c + 2 * p + 1, log2bn) : 0ull;
+          const uint64_t k = umax(k0, k1);
+          rose |= k > best;
+          best = umax(best, k);
+        }
+      }
+      // raise the warp's floor when its best key rose (warp-uniform; a NaN or -inf best
+      // leaves the floor where it is, so ties and NaNs stay exact)
+      if (__any_sync(kFull, rose)) {
+        const uint64_t wb = warp_max_u64(best);
+        if (wb > gbest) {
+          gbest = wb;
+          const float tv = bf2f((uint16_t)dec16((uint32_t)(wb >> 48)));
+          if (tv > __int_as_float(0xff800000)) gfloor = bf2f((uint16_t)(vmin_pair(tv, rc) & 0xffffu));
+        }
+      }
+      return;
+    }
     if (rc.nd.proc && ntok) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {

@@ -208,7 +208,8 @@ def config5(device, seed: int = 0, batch: int = 1024, vocab: int = 256000):
 
 def runner(name: str, device):
     """A no-argument callable that runs benchmark config `name` once through the public
-    interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep;
+    interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep; 4: three
+    cross-vocabulary greedy drafting steps and a greedy verification, as one chain;
     5: fused_singular with Philox noise; 1: UnshardedBoundedTopK)."""
     dev = torch.device(device)
     if name == "config1":
@@ -236,6 +237,28 @@ def runner(name: str, device):
         return lambda: fused_multistep(c["flat_logits"], b.flags.target, c["flat_tokens"], cu_seqlens=c["cu_seqlens"],
                                        lookahead=c["gamma"], max_top_logprobs=20, return_logprobs=True,
                                        draft_probabilities=c["probabilities"], block_n=4096, **kw)
+    if name == "config4":
+        from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
+
+        c = config4(dev, seed=10)
+        b, gamma, d2t, sm = c["buffers"], c["gamma"], c["d2t"], c["slot_mapping"]
+        active = sm.numel()
+        drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
+        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
+        # drafted tokens per slot for the drafter, gathered per request for the verifier
+        slot_tokens = torch.zeros(b.top_k.numel(), gamma + 1, dtype=I32, device=dev)
+        rows = sm.long()
+
+        def chain():
+            for t in range(gamma):
+                sel = drafter.drafting(c["draft_logits"][t], b, timestep=t, tokens=slot_tokens if t else None,
+                                       slot_mapping=sm, d2t_mapping=d2t, target_vocab=128256)
+                slot_tokens[rows, t] = sel.tokens[:, 0]
+            tokens.copy_(slot_tokens[rows])
+            return verifier(c["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
+
+        return chain
     if name == "config5":
         from sonic_sampler_b200.interface.functional.singular import fused_singular
 
