@@ -1085,19 +1085,34 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const int sg_c = sg_d + (drow ? CH * 4 : 0);
   const int sg_b = sg_c + (crow ? CH * 4 : 0);
   const int sg_g = sg_b + (brow ? CH * 2 : 0);
-  const int sg_stage = sg_g + (grow ? CH / 8 : 0);  // = the bytes of one chunk (multiple of 256)
-  const int nst = min(MAX_RING_STAGES, RING_BYTES / sg_stage);
+  const int sg_stage = sg_g + (grow ? CH / 8 : 0);  // bytes of one 2048-column chunk (multiple of 256)
+  // Greedy rows without processors (a positive temperature at most) take 4096-column chunks
+  // (8 KB) of logits: a warp then handles two adjacent groups per chunk, so the stage wait and
+  // release are paid once per 512 columns of this almost free per-column work. Such a row
+  // needs one full wide chunk (chunk 0's first half is already on its way).
+  const bool wide = MODE == kTma && (ind & 0x40) && !cand_out && !rc.nd.proc && sg_stage == CH * 2 &&
+                    (!rc.nd.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f)) && (c1 - c0) >= 2 * CH;
+  const int cw = wide ? 2 * CH : CH;                   // columns of a ring chunk
+  const int stage_bytes = wide ? 4 * CH : sg_stage;  // bytes of a ring stage
+  const int nst = min(MAX_RING_STAGES, RING_BYTES / stage_bytes);
+  const int nck = MODE == kTma ? (int)((c1 - c0) / cw) : 0;  // ring chunks of this split
   auto issue_chunk = [&](int i, int stage) {  // one thread
-    unsigned char* sp = smem_ring + stage * sg_stage;
+    unsigned char* sp = smem_ring + stage * stage_bytes;
     uint64_t* bar = &st.bars[stage];
-    const int64_t cc = c0 + (int64_t)i * CH;
+    const int64_t cc = c0 + (int64_t)i * cw;
     if (i == 0) {
-      // the logits are on their way already
-      if (sg_stage > CH * 2) mbar_expect_tx(bar, (uint32_t)(sg_stage - CH * 2));
-      else mbar_arrive(bar);
+      // the first 2048 columns' logits are on their way already
+      if (wide) {
+        mbar_expect_tx(bar, (uint32_t)(CH * 2));
+        bulk_load(sp + CH * 2, xrow + cc + CH, CH * 2, bar);
+      } else if (sg_stage > CH * 2) {
+        mbar_expect_tx(bar, (uint32_t)(sg_stage - CH * 2));
+      } else {
+        mbar_arrive(bar);
+      }
     } else {
-      mbar_expect_tx(bar, (uint32_t)sg_stage);
-      bulk_load(sp, xrow + cc, CH * 2, bar);
+      mbar_expect_tx(bar, (uint32_t)stage_bytes);
+      bulk_load(sp, xrow + cc, cw * 2, bar);
     }
     if (drow) bulk_load(sp + sg_d, drow + cc + shard, CH * 4, bar);
     if (crow) bulk_load(sp + sg_c, crow + cc + shard, CH * 4, bar);
@@ -1108,7 +1123,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     st.best = 0ull;
     st.mp = load_mask_params(P, slot);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
-    for (int i = 0; i < min(nch, nst); ++i) issue_chunk(i, i);  // barriers set up above
+    for (int i = 0; i < min(nck, nst); ++i) issue_chunk(i, i);  // barriers set up above
   }
   __syncthreads();
 
@@ -1135,35 +1150,47 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   };
 
   // exact path: every processor on every column, then the candidate test
+  // greedy keys of a group of a row without processors: under the tempered-value floor
+  // (gskip), else of the raw logits
+  auto greedy_group = [&](const Raw8& raw, int64_t c, int nvalid) {
+    if (!gskip) {
+#pragma unroll
+      for (int j = 0; j < VPT; ++j)
+        if (j < nvalid) best = umax(best, greedy_key_bits(half_of(raw.x, j), c + j, log2bn));
+      return;
+    }
+    bool rose = false;
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const float lo = bf2_lo(raw.x[p]), hi = bf2_hi(raw.x[p]);
+      const bool e0 = 2 * p < nvalid && !(lo < gfloor);
+      const bool e1 = 2 * p + 1 < nvalid && !(hi < gfloor);
+      if (e0 || e1) {
+        // the temperature step of process_pair, on this pair only
+        const uint32_t tp = rc.temp_fast ? bf2_pack(__fmul_rn(lo, rc.rtemp), __fmul_rn(hi, rc.rtemp))
+                                         : bf2_pack(__fdiv_rn(lo, rc.temp), __fdiv_rn(hi, rc.temp));
+        const uint64_t k0 = e0 ? greedy_key_bits(tp & 0xffffu, c + 2 * p, log2bn) : 0ull;
+        const uint64_t k1 = e1 ? greedy_key_bits(tp >> 16, c + 2 * p + 1, log2bn) : 0ull;
+        const uint64_t k = umax(k0, k1);
+        rose |= k > best;
+        best = umax(best, k);
+      }
+    }
+    // raise the warp's floor when its best key rose (warp-uniform; a NaN or -inf best
+    // leaves the floor where it is, so ties and NaNs stay exact)
+    if (__any_sync(kFull, rose)) {
+      const uint64_t wb = warp_max_u64(best);
+      if (wb > gbest) {
+        gbest = wb;
+        const float tv = bf2f((uint16_t)dec16((uint32_t)(wb >> 48)));
+        if (tv > __int_as_float(0xff800000)) gfloor = bf2f((uint16_t)(vmin_pair(tv, rc) & 0xffffu));
+      }
+    }
+  };
+
   auto exact_group = [&](Raw8& raw, int64_t c, int nvalid) {
     if (gskip) {
-      bool rose = false;
-#pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        const float lo = bf2_lo(raw.x[p]), hi = bf2_hi(raw.x[p]);
-        const bool e0 = 2 * p < nvalid && !(lo < gfloor);
-        const bool e1 = 2 * p + 1 < nvalid && !(hi < gfloor);
-        if (e0 || e1) {
-          // the temperature step of process_pair, on this pair only
-          const uint32_t tp = rc.temp_fast ? bf2_pack(__fmul_rn(lo, rc.rtemp), __fmul_rn(hi, rc.rtemp))
-                                           : bf2_pack(__fdiv_rn(lo, rc.temp), __fdiv_rn(hi, rc.temp));
-          const uint64_t k0 = e0 ? greedy_key_bits(tp & 0xffffu, c + 2 * p, log2bn) : 0ull;
-          const uint64_t k1 = e1 ? greedy_key_bits(tp >> 16, c + 2 * p + 1, log2bn) : 0ull;
-          const uint64_t k = umax(k0, k1);
-          rose |= k > best;
-          best = umax(best, k);
-        }
-      }
-      // raise the warp's floor when its best key rose (warp-uniform; a NaN or -inf best
-      // leaves the floor where it is, so ties and NaNs stay exact)
-      if (__any_sync(kFull, rose)) {
-        const uint64_t wb = warp_max_u64(best);
-        if (wb > gbest) {
-          gbest = wb;
-          const float tv = bf2f((uint16_t)dec16((uint32_t)(wb >> 48)));
-          if (tv > __int_as_float(0xff800000)) gfloor = bf2f((uint16_t)(vmin_pair(tv, rc) & 0xffffu));
-        }
-      }
+      greedy_group(raw, c, nvalid);
       return;
     }
     if (rc.nd.proc && ntok) {
@@ -1282,7 +1309,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   constexpr int DM = MODE == kTma ? kVec : MODE;  // direct loads
 
   // chunk k (full 2048-column chunks only) is group k * NW + warp of every warp
-  const int nchunks = MODE == kTma ? (int)((c1 - c0) / CH) : 0;
+  const int nchunks = wide ? 0 : nck;  // chunks of the standard layout
   bool werr = false;
   if (MODE == kTma && rc.fast && !greedy && nchunks > 0) {
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
@@ -1324,14 +1351,44 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
   int stage = 0;
   uint32_t phase = 0;
-  for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
+  // wide chunks (greedy rows): groups 2 * NW * k + 2 * warp and the next one
+  for (int k = 0; k < (wide ? nck : 0); ++k) {
+    if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+    const unsigned char* sp = smem_ring + stage * stage_bytes + warp * (GROUP * 4) + lane * 16;
+    const int g0 = 2 * NW * k + 2 * warp;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      Raw8 raw;
+      const uint4 xq = *reinterpret_cast<const uint4*>(sp + h * (GROUP * 2));
+      raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
+      greedy_group(raw, gcol(g0 + h), VPT);
+    }
+    __syncwarp();
+    if (lane == 0) {
+      __threadfence_block();
+      if (atomicAdd(&st.rel[stage], 1) == NW - 1) {
+        atomicExch(&st.rel[stage], 0);
+        if (k + nst < nck) {
+          __threadfence_block();
+          fence_proxy_async();
+          issue_chunk(k + nst, stage);
+        }
+      }
+    }
+    if (++stage == nst) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+  // the remaining groups: standard ring chunks, then direct loads
+  for (int k = 0, g = (wide ? 2 * NW * nck : 0) + warp; g < ngroups; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     Raw8 raw;
     const bool staged = k < nchunks;
     if (staged) {
       if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
-      const unsigned char* sp = smem_ring + stage * sg_stage;
+      const unsigned char* sp = smem_ring + stage * stage_bytes;
       const uint4 xq = *reinterpret_cast<const uint4*>(sp + warp * (GROUP * 2) + lane * 16);
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
 #pragma unroll
