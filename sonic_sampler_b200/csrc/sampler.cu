@@ -1080,12 +1080,18 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const int32_t* drow = rc.nd.dec ? P.decode_counts + slot * P.counts_stride : nullptr;
   const int32_t* crow = rc.nd.ctx ? P.context_counts + slot * P.counts_stride : nullptr;
   const uint16_t* brow = rc.nd.bias ? P.bias + slot * P.bias_stride : nullptr;
-  // stage layout of this row: only the streams it reads, as many stages as fit the ring
+  // stage layout of this row: only the streams it reads, as many stages as fit the ring. With a
+  // draft-to-target table (INDIRECT) the ring carries the logits alone: the aux rows are
+  // indexed by target id, so those values are gathered per group instead.
+  const int32_t* rdrow = INDIRECT ? nullptr : drow;
+  const int32_t* rcrow = INDIRECT ? nullptr : crow;
+  const uint16_t* rbrow = INDIRECT ? nullptr : brow;
+  const uint32_t* rgrow = INDIRECT ? nullptr : grow;
   const int sg_d = CH * 2;
-  const int sg_c = sg_d + (drow ? CH * 4 : 0);
-  const int sg_b = sg_c + (crow ? CH * 4 : 0);
-  const int sg_g = sg_b + (brow ? CH * 2 : 0);
-  const int sg_stage = sg_g + (grow ? CH / 8 : 0);  // bytes of one 2048-column chunk (multiple of 256)
+  const int sg_c = sg_d + (rdrow ? CH * 4 : 0);
+  const int sg_b = sg_c + (rcrow ? CH * 4 : 0);
+  const int sg_g = sg_b + (rbrow ? CH * 2 : 0);
+  const int sg_stage = sg_g + (rgrow ? CH / 8 : 0);  // bytes of one 2048-column chunk (multiple of 256)
   // Greedy rows without processors (a positive temperature at most) take 4096-column chunks
   // (8 KB) of logits: a warp then handles two adjacent groups per chunk, so the stage wait and
   // release are paid once per 512 columns of this almost free per-column work. Such a row
@@ -1114,10 +1120,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       mbar_expect_tx(bar, (uint32_t)stage_bytes);
       bulk_load(sp, xrow + cc, cw * 2, bar);
     }
-    if (drow) bulk_load(sp + sg_d, drow + cc + shard, CH * 4, bar);
-    if (crow) bulk_load(sp + sg_c, crow + cc + shard, CH * 4, bar);
-    if (brow) bulk_load(sp + sg_b, brow + cc + shard, CH * 2, bar);
-    if (grow) bulk_load(sp + sg_g, grow + (cc + shard) / 32, CH / 8, bar);
+    if (rdrow) bulk_load(sp + sg_d, rdrow + cc + shard, CH * 4, bar);
+    if (rcrow) bulk_load(sp + sg_c, rcrow + cc + shard, CH * 4, bar);
+    if (rbrow) bulk_load(sp + sg_b, rbrow + cc + shard, CH * 2, bar);
+    if (rgrow) bulk_load(sp + sg_g, rgrow + (cc + shard) / 32, CH / 8, bar);
   };
   if (tid == 0) {
     st.best = 0ull;
@@ -1311,7 +1317,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   // chunk k (full 2048-column chunks only) is group k * NW + warp of every warp
   const int nchunks = wide ? 0 : nck;  // chunks of the standard layout
   bool werr = false;
-  if (MODE == kTma && rc.fast && !greedy && nchunks > 0) {
+  if (MODE == kTma && rc.fast && !greedy && nchunks > 0 && !(INDIRECT && rc.nd.proc)) {
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
     // columns whose counts are zero and that hold no drafted token (their value needs no
     // penalty), bound 128 distinct keys.
@@ -1396,25 +1402,36 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 #pragma unroll
       for (int p = 0; p < 4; ++p) raw.b[p] = 0;
       raw.g = 0xffu;
-      if (drow) {
+      if (INDIRECT && rc.nd.proc) {
+        // aux values of the group's target ids, gathered as the direct path does
+        int64_t col[VPT];
+#pragma unroll
+        for (int j = 0; j < VPT; ++j) {
+          col[j] = c + j + a.shard_offset;
+          if (j < nv) col[j] = load_index(a.d2t, a.d2t_dtype, col[j]);
+        }
+        load_aux8<kScalar>(a.params, rc, slot, col, nv, raw);
+        if (rc.nd.g) raw.g = load_g8<kScalar>(a.params, gslot, col, nv);
+      }
+      if (rdrow) {
         const unsigned char* dp = sp + sg_d + warp * (GROUP * 4) + lane * 32;
         const uint4 u = *reinterpret_cast<const uint4*>(dp);
         const uint4 v = *reinterpret_cast<const uint4*>(dp + 16);
         raw.d[0] = u.x; raw.d[1] = u.y; raw.d[2] = u.z; raw.d[3] = u.w;
         raw.d[4] = v.x; raw.d[5] = v.y; raw.d[6] = v.z; raw.d[7] = v.w;
       }
-      if (crow) {
+      if (rcrow) {
         const unsigned char* cp = sp + sg_c + warp * (GROUP * 4) + lane * 32;
         const uint4 u = *reinterpret_cast<const uint4*>(cp);
         const uint4 v = *reinterpret_cast<const uint4*>(cp + 16);
         raw.c[0] = u.x; raw.c[1] = u.y; raw.c[2] = u.z; raw.c[3] = u.w;
         raw.c[4] = v.x; raw.c[5] = v.y; raw.c[6] = v.z; raw.c[7] = v.w;
       }
-      if (brow) {
+      if (rbrow) {
         const uint4 u = *reinterpret_cast<const uint4*>(sp + sg_b + warp * (GROUP * 2) + lane * 16);
         raw.b[0] = u.x; raw.b[1] = u.y; raw.b[2] = u.z; raw.b[3] = u.w;
       }
-      if (grow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
+      if (rgrow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
     } else {
       load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, c, nv, raw);
     }
@@ -2413,7 +2430,8 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     return check_launch(pe, what);
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
-  if (mode == kVec && !ind && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
+  // with a d2t table the ring streams the logits only, which xvec already allows
+  if (mode == kVec && (ind || params_tma_ok(a->params, a->shard_offset))) mode = kTma;
   dim3 grid(p.splits, a->rows);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
@@ -2421,8 +2439,9 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   const size_t ring = mode == kTma ? (size_t)RING_BYTES : 0;
   cudaError_t e;
   if (ind)
-    e = mode == kVec ? launch(singular_kernel<kVec, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
-                     : launch(singular_kernel<kScalar, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
+    e = mode == kTma  ? launch(singular_kernel<kTma, true, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
+        : mode == kVec ? launch(singular_kernel<kVec, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
+                       : launch(singular_kernel<kScalar, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
   else if (mode == kTma)
     e = launch(singular_kernel<kTma, false, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
   else
