@@ -628,3 +628,36 @@ def test_multistep_philox_residual_distribution(dev):
     expected = p.double() * requests
     chi2 = float(((counts - expected) ** 2 / expected).sum())
     assert chi2 < 24.32, (chi2, counts.tolist(), expected.tolist())  # 7 dof, P = 0.001
+
+
+def test_greedy_temperature_floor_edges(dev):
+    """Greedy rows whose only processor is a temperature take the tempered-value floor (and,
+    on 4096-column splits, wide ring chunks): ties made by the division, NaN logits, an all
+    -inf row, tied +inf values, a +-0 maximum and both temperature paths (divide, exact
+    reciprocal) must match the oracle bit for bit."""
+    V, rows = 128256, 8
+    b = _params(dev, rows, V, seed=41, processors=False)
+    x = workloads.peaked_logits(rows, V, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=41)
+    g = torch.Generator().manual_seed(41)
+    # row 1: many near-maximal values that collapse to one bf16 after dividing by 3
+    near = torch.randperm(V, generator=g)[:64]
+    x[1, near] = (torch.full((64,), 20.0) + torch.arange(64) * 0.0625).to(BF16).to(dev)
+    # row 2: NaNs among the logits
+    x[2, torch.randperm(V, generator=g)[:5]] = float("nan")
+    # row 3: every logit -inf
+    x[3] = float("-inf")
+    # row 4: two +inf values in different tiles
+    x[4, 777] = float("inf")
+    x[4, 90001] = float("inf")
+    # row 5: all negative but a -0.0 and a +0.0
+    x[5] = -x[5].abs() - 1.0
+    x[5, 5000] = -0.0
+    x[5, 70000] = 0.0
+    kw = buffer_kwargs(b)
+    ind = torch.full((rows,), 0x60, dtype=torch.uint16)  # greedy + temperature
+    ind[7] = 0x40  # greedy without temperature
+    kw["indicators"] = ind.to(dev)
+    temp = torch.tensor([0.7, 3.0, 0.9, 1.3, 0.6, 0.8, 0.5, 1.1], dtype=BF16)
+    kw["temperature"] = temp.to(dev)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
