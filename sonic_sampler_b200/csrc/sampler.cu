@@ -776,6 +776,12 @@ __device__ __forceinline__ uint32_t vmin_pair(float thr, const RowConsts& rc) {
   return vmin_pair(thr, rc.nd.temp, rc.temp_fast, rc.temp, rc.rtemp);
 }
 
+// Floor of a greedy row whose only processor is its temperature: the smallest bf16 logit whose
+// tempered value is at least tv (out of line: it runs only when a warp's best key rises).
+__device__ __noinline__ float greedy_floor(float tv, bool fast, float t, float rt) {
+  return bf2f((uint16_t)(vmin_pair(tv, true, fast, t, rt) & 0xffffu));
+}
+
 // How many leading candidates of a row can ever matter: with top-k (k < 128) set, positions
 // >= k are masked to -inf before top-p, min-p, the softmax and the selection, so only the
 // exact top-k is needed (and the cut may come from the k-th key), unless top-Z logprobs
@@ -1189,7 +1195,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       if (wb > gbest) {
         gbest = wb;
         const float tv = bf2f((uint16_t)dec16((uint32_t)(wb >> 48)));
-        if (tv > __int_as_float(0xff800000)) gfloor = bf2f((uint16_t)(vmin_pair(tv, rc) & 0xffffu));
+        if (tv > __int_as_float(0xff800000)) gfloor = greedy_floor(tv, rc.temp_fast, rc.temp, rc.rtemp);
       }
     }
   };
@@ -1362,7 +1368,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
     const unsigned char* sp = smem_ring + stage * stage_bytes + warp * (GROUP * 4) + lane * 16;
     const int g0 = 2 * NW * k + 2 * warp;
-#pragma unroll
+#pragma unroll 1
     for (int h = 0; h < 2; ++h) {
       Raw8 raw;
       const uint4 xq = *reinterpret_cast<const uint4*>(sp + h * (GROUP * 2));
