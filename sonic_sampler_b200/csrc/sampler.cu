@@ -1564,14 +1564,15 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 // plain singular rows: no grammar, counts, bias, d2t or drafted tokens anywhere in the call
 // (logits, optional temperature, then the usual masking and selection). Same machinery as
 // singular_kernel with wider groups: 16 columns a lane, 512 a warp, 4096-column chunks of
-// logits only (8 KB a stage; 5 stages and 3 CTAs an SM for grids of several waves, else 9).
+// logits only (8 KB a stage; 3 stages and 4 CTAs an SM for grids of several waves, else 9 stages
+// and 3 CTAs).
 // ---------------------------------------------------------------------------------------
 
 constexpr int PVPT = 16;               // columns per lane
 constexpr int PGROUP = PVPT * 32;      // columns per warp group
 constexpr int PCH = PGROUP * NW;       // columns per chunk
 constexpr int PSTAGE = PCH * 2;        // bytes per stage
-constexpr int PNST_WAVES = 5;         // ring stages of a multi-wave grid: 40 KB, 3 CTAs an SM
+constexpr int PNST_WAVES = 3;         // ring stages of a multi-wave grid: 24 KB, 4 CTAs an SM
 constexpr int PNST_ONE = 9;           // of a one-wave grid: 72 KB, more bytes in flight a CTA
 constexpr int PQCAP = kMaxK + PGROUP;  // a warp appends at most 512 keys per group
 
@@ -1597,8 +1598,10 @@ __device__ __forceinline__ uint32_t half16(const uint32_t (&x)[8], int j) {
   return (j & 1) ? (w >> 16) : (w & 0xffffu);
 }
 
-template <int MODE>
-__global__ void __launch_bounds__(NT, 3) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
+// MINB: CTAs an SM the registers are budgeted for (4 for grids of several waves, whose CTAs'
+// fixed costs then overlap more; 3 for one-wave grids, which take a deeper ring instead)
+template <int MODE, int MINB>
+__global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, int nst) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
@@ -2426,13 +2429,16 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     const dim3 pgrid(p.splits, a->rows);
     const bool ppdl = (a->flags & SONIC_FLAG_PDL) != 0;
     const int pl2 = ilog2(a->block_n);
-    // a grid of several waves keeps 3 CTAs an SM busy (their fixed costs overlap); one wave
-    // streams longer rows per CTA and takes a deeper ring instead
-    const int nst = (int64_t)p.splits * a->rows > TARGET_CTAS ? PNST_WAVES : PNST_ONE;
+    // a grid of several waves keeps 4 CTAs an SM busy with a 3-stage ring (their fixed costs
+    // overlap); one wave streams longer rows per CTA and takes 3 CTAs with a deeper ring
+    const bool waves = (int64_t)p.splits * a->rows > TARGET_CTAS;
+    const int nst = waves ? PNST_WAVES : PNST_ONE;
+    cudaStream_t pst = (cudaStream_t)stream;
+    const size_t pring = (size_t)nst * PSTAGE;
     const cudaError_t pe =
-        pm == kTma ? launch(plain_kernel<kTma>, pgrid, (size_t)nst * PSTAGE, (cudaStream_t)stream, ppdl, *a, p.splits,
-                            p.cols, pl2, ws, nst)
-                   : launch(plain_kernel<kScalar>, pgrid, 0, (cudaStream_t)stream, ppdl, *a, p.splits, p.cols, pl2, ws, 0);
+        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst)
+                            : launch(plain_kernel<kTma, 3>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst))
+                   : launch(plain_kernel<kScalar, 3>, pgrid, 0, pst, ppdl, *a, p.splits, p.cols, pl2, ws, 0);
     return check_launch(pe, what);
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
