@@ -55,6 +55,7 @@ struct Plan {
 // Column split of a unit (row or request) of V columns; a pure function of the shapes, so
 // the workspace size never depends on the device.
 static Plan split_plan(int64_t units, int64_t V, int chunk) {
+  if (V <= 0) return Plan{1, chunk};  // no columns: callers reject such calls before launching
   int64_t s = units > 0 ? TARGET_CTAS / units : 1;
   s = std::max<int64_t>(s, 1);
   s = std::max<int64_t>(s, (V + MAX_SPLIT_COLS - 1) / MAX_SPLIT_COLS);
@@ -2366,17 +2367,17 @@ int32_t sonic_abi_version(void) { return SONIC_B200_ABI_VERSION; }
 const char* sonic_last_error(void) { return g_last_error.c_str(); }
 
 size_t sonic_fused_singular_workspace_size(const SonicSingularArgs* a) {
-  if (!a || a->rows <= 0) return 0;
+  if (!a || a->rows <= 0 || a->vocab_size < kMaxK) return 0;
   return workspace_bytes(a->rows, a->rows, singular_plan(a->rows, a->vocab_size).splits);
 }
 
 size_t sonic_fused_multistep_workspace_size(const SonicMultistepArgs* a) {
-  if (!a || a->batch_size <= 0) return 0;
+  if (!a || a->batch_size <= 0 || a->vocab_size < kMaxK) return 0;
   return workspace_bytes(multistep_rows(a), a->batch_size, multistep_plan(multistep_rows(a), a->vocab_size).splits);
 }
 
 size_t sonic_bounded_topk_workspace_size(const SonicTopKArgs* a) {
-  if (!a || a->rows <= 0) return 0;
+  if (!a || a->rows <= 0 || a->vocab_size < kMaxK) return 0;
   return workspace_bytes(a->rows, a->rows, singular_plan(a->rows, a->vocab_size).splits);
 }
 
@@ -3019,6 +3020,10 @@ static sonic_status static_scratch(void** out) {
 extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, void* stream) {
   if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
   if (a->rows == 0) return SONIC_OK;
+  // every argument check runs before the scratch is sized, carved or cleared
+  if (sonic_status s = check_singular(a, true)) return s;
+  if (!a->logits || a->logits_dtype != SONIC_DTYPE_BF16)
+    return fail(SONIC_ERR_INVALID_ARGUMENT, "logits must be a non-NULL bf16 tensor");
   const size_t need = sonic_fused_singular_workspace_size(a);
   if (need > kStaticScratchBytes)
     return fail(SONIC_ERR_WORKSPACE, "sonic_fused_singular_static: this call needs " + std::to_string(need) +
@@ -3030,6 +3035,7 @@ extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, 
   const Plan p = singular_plan(a->rows, a->vocab_size);
   const Workspace ws = carve(base, a->rows, a->rows, p.splits);
   const size_t off = (size_t)((char*)ws.tickets - (char*)base);
+  if (off >= need) return fail(SONIC_ERR_UNSUPPORTED, "sonic_fused_singular_static: scratch layout");
   const cudaError_t e = cudaMemsetAsync(ws.tickets, 0, need - off, (cudaStream_t)stream);
   if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("sonic_fused_singular_static: ") + cudaGetErrorString(e));
   SonicSingularArgs b = *a;

@@ -108,6 +108,27 @@ def test_host_validation_without_gpu(lib):
     assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "power of two" in msg
 
 
+def test_static_entry_validates_before_touching_scratch(lib):
+    """sonic_fused_singular_static checks every argument before it sizes, carves or clears its
+    scratch: bad shapes return SONIC_ERR_INVALID_ARGUMENT and an oversize call
+    SONIC_ERR_WORKSPACE, with no CUDA call made (so this runs on machines without a GPU)."""
+    a = _abi.SingularArgs()
+    a.rows, a.vocab_size, a.block_n = -1, 128256, 4096
+    st, msg = _status(lib, "sonic_fused_singular_static", a)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "rows" in msg
+    a.rows, a.vocab_size = 4, 0
+    st, msg = _status(lib, "sonic_fused_singular_static", a)
+    assert st == _abi.SONIC_ERR_INVALID_ARGUMENT and "vocab_size" in msg
+    assert lib.sonic_fused_singular_workspace_size(ctypes.byref(a)) == 0  # no division by the empty vocabulary
+    # arguments that pass every check but need more than the 4 MiB scratch; the pointers are
+    # never dereferenced because the size check fails first
+    fake = 1 << 20
+    a.rows, a.vocab_size = 4096, 128256
+    a.params.indicators = a.tokens = a.gumbel = a.logits = fake
+    st, msg = _status(lib, "sonic_fused_singular_static", a)
+    assert st == _abi.SONIC_ERR_WORKSPACE and "static scratch" in msg
+
+
 def test_update_counts_without_decode_counts_message(lib):
     """Same message as the reference's runtime check (functional/base.py:34-38)."""
     import torch

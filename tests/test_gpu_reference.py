@@ -1,0 +1,285 @@
+"""CUDA path against the reference's own Triton kernels, run unmodified on the same B200 on
+identical device inputs (tests/reference_gpu.py says where the reference comes from).
+
+This pins parity to the reference as deployed: its libdevice fast exp/log and whatever
+multiply-add contraction Triton applies on sm_100. The bar, per output:
+- tokens, top-k indices, acceptance offsets, decode counts: bit for bit;
+- logprobs: the reference writes bf16; our kernels run once more with fp32 logprobs, and the
+  reference's bf16 value must be a round-to-nearest bf16 of some fp32 value within 1e-5 of
+  ours (the 1e-5 fp32 tolerance, seen through the reference's bf16 output);
+- multistep stage-2 probabilities (fp32): within 1e-5 absolute, candidate indices bit for bit.
+
+Each test prints how many rows differ in any way, for the record.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+from sonic_sampler_b200 import workloads
+
+pytestmark = pytest.mark.gpu
+
+BF16, F32, I32 = torch.bfloat16, torch.float32, torch.int32
+TOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def ref():
+    if not torch.cuda.is_available():
+        pytest.skip("needs CUDA")
+    from tests import reference_gpu
+
+    why = reference_gpu.unavailable()
+    if why:
+        pytest.skip(why)
+    from sonic_sampler_b200 import _abi
+
+    _abi.load_library()
+    torch.cuda.set_device(0)
+    return reference_gpu.load()
+
+
+@pytest.fixture(scope="module")
+def dev(ref):
+    return torch.device("cuda", 0)
+
+
+def lp_within(ref_bf16: torch.Tensor, ours_f32: torch.Tensor, tol: float = TOL) -> torch.Tensor:
+    """Elementwise: is the reference's bf16 logprob RN_bf16(x) for some x within `tol` of ours?"""
+    r = ref_bf16.float().cpu()
+    o = ours_f32.float().cpu()
+    lo = (o - tol).to(BF16).float()
+    hi = (o + tol).to(BF16).float()
+    ok = (r >= lo) & (r <= hi)
+    return ok | (torch.isnan(r) & torch.isnan(o))
+
+
+def report(name: str, **counts):
+    print(f"[reference parity] {name}: " + ", ".join(f"{k}={v}" for k, v in counts.items()), flush=True)
+
+
+def singular_kwargs(b, draft: bool = False, timestep: int = 0) -> dict:
+    g = b.weights.gumbel.draft if draft else b.weights.gumbel.target
+    return dict(
+        indicators=b.flags.draft if draft else b.flags.target, grammar=b.grammar[:, timestep],
+        context_counts=b.repetition.counts.context, decode_counts=b.repetition.counts.decode,
+        repetition_penalties=b.repetition.multiplicative, frequency_penalties=b.repetition.frequency,
+        presence_penalties=b.repetition.presence, logit_bias=b.bias, temperature=b.temperature, top_k=b.top_k,
+        top_p=b.top_p, min_p=b.min_p, top_k_logprobs=b.top_logprobs, gumbel_noise=g[:, timestep],
+    )
+
+
+# ----------------------------------------------------------------------------------------
+# config 1: UnshardedBoundedTopK (bf16, the reference's only logits dtype)
+# ----------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("k", [32, 128])
+def test_config1_topk_matches_reference(ref, dev, k):
+    from sonic_sampler_b200.interface import UnshardedBoundedTopK
+
+    c = workloads.config1(dev)
+    x = c["logits"].to(BF16)
+    with torch.device(dev):
+        theirs = ref.UnshardedBoundedTopK.initialize(32000, batch_size=8, k=k).clear()
+    ours = UnshardedBoundedTopK.initialize(32000, batch_size=8, k=k).clear()
+    tv, ti = theirs(x)
+    ov, oi = ours(x)
+    torch.cuda.synchronize()
+    n = 8 * k  # both write row r's k results at flat offset r*k (reference quirk Q1)
+    tv, ti = tv.reshape(-1)[:n].cpu(), ti.reshape(-1)[:n].cpu()
+    ov, oi = ov.reshape(-1)[:n].cpu(), oi.reshape(-1)[:n].cpu()
+    report(f"config1 k={k}", index_mismatch=int((ti != oi).sum()), value_mismatch=int((tv.view(torch.int16) != ov.view(torch.int16)).sum()))
+    assert torch.equal(ti, oi)
+    assert torch.equal(tv.view(torch.int16), ov.view(torch.int16))
+
+
+# ----------------------------------------------------------------------------------------
+# config 2: UnshardedFusedSingular.autoregressive, every processor, heterogeneous rows
+# ----------------------------------------------------------------------------------------
+
+
+def _config2_case(ref, dev, w, name: str):
+    from sonic_sampler_b200.interface import UnshardedFusedSingular
+    from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+    logits = w["logits"]
+    rows, vocab = logits.shape
+    b_ref, b_ours, b_f32 = w["buffers"].to(dev), w["buffers"].to(dev), w["buffers"].to(dev)
+    with torch.device(dev):
+        theirs = ref.UnshardedFusedSingular.initialize(vocab, batch_size=rows)
+    ours = UnshardedFusedSingular.initialize(vocab, batch_size=rows)
+    assert ours.block_n == theirs.block_n  # same tile width: the greedy tie rule depends on it
+    ts = theirs.autoregressive(logits, b_ref, update_counts=True, logprobs=True)
+    os_ = ours.autoregressive(logits, b_ours, update_counts=True, logprobs=True)
+    # our fp32 logprobs of the same call, for the tolerance check
+    of = fused_singular(logits, **singular_kwargs(b_f32), block_n=ours.block_n, return_logprobs=True,
+                        max_top_logprobs=ours.max_top_logprobs, logprobs_dtype=F32)
+    torch.cuda.synchronize()
+
+    stoch = ~(b_ref.flags.target.cpu().to(I32) & 0x40).bool()
+    tok_bad = (ts.tokens.cpu() != os_.tokens.cpu()).view(-1)
+    cnt_bad = (b_ref.repetition.counts.decode != b_ours.repetition.counts.decode).any(dim=1).cpu()
+    lp_ok = lp_within(ts.logprobs.selected, of.logprobs.selected).view(-1)
+    lp_bits = (ts.logprobs.selected.cpu().view(torch.int16) != os_.logprobs.selected.cpu().view(torch.int16)).view(-1)
+    z = ours.max_top_logprobs
+    zmask = torch.zeros(rows, z, dtype=torch.bool)
+    for r in range(rows):
+        ind = int(b_ref.flags.target[r])
+        if stoch[r] and ind & 0x400:
+            zmask[r, : min(int(b_ref.top_logprobs[r]), z)] = True
+    ztok_bad = ((ts.logprobs.top_k.tokens.cpu() != os_.logprobs.top_k.tokens.cpu()) & zmask).any(dim=1)
+    zlp_ok = (lp_within(ts.logprobs.top_k.logprobs, of.logprobs.top_k.logprobs) | ~zmask).all(dim=1)
+    report(name, rows=rows, token_mismatch=int(tok_bad.sum()), count_rows_mismatch=int(cnt_bad.sum()),
+           logprob_outside_1e5=int((~lp_ok & stoch).sum()), logprob_bf16_bits_differ=int((lp_bits & stoch).sum()),
+           topz_token_mismatch=int(ztok_bad.sum()), topz_logprob_outside_1e5=int((~zlp_ok).sum()))
+    assert not tok_bad.any(), tok_bad.nonzero().flatten().tolist()
+    assert not cnt_bad.any()
+    assert bool(lp_ok[stoch].all())
+    assert not ztok_bad.any() and bool(zlp_ok.all())
+
+
+@pytest.mark.parametrize("seed", [5, 6])
+def test_config2_matches_reference(ref, dev, seed):
+    _config2_case(ref, dev, workloads.config2(dev, seed=seed), f"config2 seed={seed}")
+
+
+def test_config2_mixed_greedy_matches_reference(ref, dev):
+    """A third of the rows greedy (with every processor): the reference's greedy tile rule."""
+    w = workloads.config2(dev, seed=11)
+    packed = w["buffers"].flags.packed
+    packed[::3, 0] |= 0x40
+    w["buffers"].flags.target_host = [int(v) for v in packed[:, 0].tolist()]
+    _config2_case(ref, dev, w, "config2 mixed greedy")
+
+
+def test_config2_top_logprobs_matches_reference(ref, dev):
+    """Rows asking for top-Z logprobs (indicator bit 0x400), Z = 5."""
+    w = workloads.config2(dev, seed=12)
+    b = w["buffers"]
+    b.top_logprobs.fill_(5)
+    b.flags.packed[:, 0] |= 0x400
+    b.flags.target_host = [int(v) for v in b.flags.packed[:, 0].tolist()]
+    _config2_case(ref, dev, w, "config2 top-5 logprobs")
+
+
+# ----------------------------------------------------------------------------------------
+# config 3: fused_multistep, varlen stochastic verification with fp32 draft probabilities
+# ----------------------------------------------------------------------------------------
+
+
+def _multistep_kwargs(b) -> dict:
+    return dict(
+        grammar=b.grammar, context_counts=b.repetition.counts.context, decode_counts=b.repetition.counts.decode,
+        repetition_penalties=b.repetition.multiplicative, frequency_penalties=b.repetition.frequency,
+        presence_penalties=b.repetition.presence, logit_bias=b.bias, temperature=b.temperature, top_k=b.top_k,
+        top_p=b.top_p, min_p=b.min_p, top_k_logprobs=b.top_logprobs, gumbel_noise=b.weights.gumbel.target,
+        uniform_noise=b.weights.uniform,
+    )
+
+
+@pytest.mark.parametrize("varlen,q_dtype", [(True, F32), (False, BF16)])
+def test_config3_matches_reference(ref, dev, varlen, q_dtype):
+    from sonic_sampler_b200.interface.functional.multistep import fused_multistep
+
+    c = workloads.config3(dev, seed=8, varlen=varlen)
+    gamma, vocab = c["gamma"], 128256
+    q = c["probabilities"].to(q_dtype)
+    if varlen:
+        logits, tokens, extra = c["flat_logits"], c["flat_tokens"], dict(cu_seqlens=c["cu_seqlens"])
+    else:
+        logits, tokens, extra = c["logits"], c["tokens"], {}
+    rows = logits.reshape(-1, vocab).size(0)
+    batch = c["tokens"].size(0)
+    out = {}
+    for who in ("theirs", "ours", "ours_f32"):
+        b = c["buffers"].to(dev)
+        vals = torch.zeros(rows, 128, dtype=F32, device=dev)
+        idx = torch.full((rows, 128), -1, dtype=I32, device=dev)
+        kw = dict(lookahead=gamma, max_top_logprobs=20, return_logprobs=True, update_counts=True,
+                  draft_probabilities=q, block_n=4096, values=vals, indices=idx, **extra, **_multistep_kwargs(b))
+        if who == "theirs":
+            v = ref.fused_multistep(logits, b.flags.target, tokens.clone(), **kw)
+        else:
+            if who == "ours_f32":
+                kw["logprobs_dtype"] = F32
+            v = fused_multistep(logits, b.flags.target, tokens.clone(), **kw)
+        out[who] = (v, vals, idx, b)
+    torch.cuda.synchronize()
+    (tv, tvals, tidx, tb), (ov, ovals, oidx, ob), (fv, _, _, _) = out["theirs"], out["ours"], out["ours_f32"]
+    off_t, off_o = tv.offsets.cpu().view(-1), ov.offsets.cpu().view(-1)
+    tok_bad = (tv.tokens.cpu() != ov.tokens.cpu())
+    cnt_bad = (tb.repetition.counts.decode != ob.repetition.counts.decode).any(dim=1).cpu()
+    # stage-2 buffers: fp32 probabilities within 1e-5, candidate ids exact (every row is stochastic)
+    prob_bad = ((tvals - ovals).abs() > TOL).any(dim=1).cpu()
+    idx_bad = (tidx != oidx).any(dim=1).cpu()
+    # logprobs and top-20 only for steps <= accepted (reference quirk Q12)
+    if varlen:
+        cu = c["cu_seqlens"].cpu()
+        pos = [(int(cu[b]) + s) for b in range(batch) for s in range(int(off_t[b]) + 1)]
+        lp_t = tv.logprobs.selected.cpu()[pos]
+        lp_f = fv.logprobs.selected.cpu()[pos]
+        zt_t, zt_o = tv.logprobs.top_k.tokens.cpu()[pos], ov.logprobs.top_k.tokens.cpu()[pos]
+        zl_t, zl_f = tv.logprobs.top_k.logprobs.cpu()[pos], fv.logprobs.top_k.logprobs.cpu()[pos]
+    else:
+        m = torch.arange(gamma + 1)[None, :] <= off_t[:, None]
+        lp_t, lp_f = tv.logprobs.selected.cpu()[m], fv.logprobs.selected.cpu()[m]
+        zt_t, zt_o = tv.logprobs.top_k.tokens.cpu()[m], ov.logprobs.top_k.tokens.cpu()[m]
+        zl_t, zl_f = tv.logprobs.top_k.logprobs.cpu()[m], fv.logprobs.top_k.logprobs.cpu()[m]
+    lp_ok = lp_within(lp_t, lp_f)
+    zl_ok = lp_within(zl_t, zl_f)
+    report(f"config3 varlen={varlen} q={q_dtype}", requests=batch, rows=rows,
+           offset_mismatch=int((off_t != off_o).sum()), token_mismatch=int(tok_bad.sum()),
+           count_rows_mismatch=int(cnt_bad.sum()), stage2_prob_rows_outside_1e5=int(prob_bad.sum()),
+           stage2_index_rows_mismatch=int(idx_bad.sum()), logprob_outside_1e5=int((~lp_ok).sum()),
+           topz_token_mismatch=int((zt_t != zt_o).sum()), topz_logprob_outside_1e5=int((~zl_ok).sum()),
+           max_stage2_prob_diff=float((tvals - ovals).abs().max()))
+    assert torch.equal(off_t, off_o)
+    assert not tok_bad.any()
+    assert not cnt_bad.any()
+    assert not idx_bad.any()
+    assert not prob_bad.any()
+    assert bool(lp_ok.all()) and torch.equal(zt_t, zt_o) and bool(zl_ok.all())
+
+
+# ----------------------------------------------------------------------------------------
+# config 4: Eagle-3 cross-vocabulary greedy drafting with slot indirection + greedy verification
+# ----------------------------------------------------------------------------------------
+
+
+def test_config4_chain_matches_reference(ref, dev):
+    from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
+
+    c = workloads.config4(dev, seed=10)
+    gamma, d2t, sm = c["gamma"], c["d2t"], c["slot_mapping"]
+    active = sm.numel()
+    rows = sm.long()
+    results = {}
+    for who in ("theirs", "ours"):
+        b = c["buffers"].to(dev)
+        if who == "theirs":
+            with torch.device(dev):
+                drafter = ref.UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
+                verifier = ref.UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        else:
+            drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
+            verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        slot_tokens = torch.zeros(b.top_k.numel(), gamma + 1, dtype=I32, device=dev)
+        drafted = []
+        for t in range(gamma):
+            sel = drafter.drafting(c["draft_logits"][t], b, timestep=t, tokens=slot_tokens if t else None,
+                                   slot_mapping=sm, d2t_mapping=d2t, target_vocab=128256)
+            slot_tokens[rows, t] = sel.tokens[:, 0]
+            drafted.append(sel.tokens[:, 0].clone())
+        tokens = slot_tokens[rows].contiguous()
+        v = verifier(c["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
+        results[who] = (torch.stack(drafted).cpu(), v.tokens.cpu().clone(), v.offsets.cpu().clone())
+    torch.cuda.synchronize()
+    (td, tt, to), (od, ot, oo) = results["theirs"], results["ours"]
+    report("config4 chain", requests=active, drafted_mismatch=int((td != od).sum()),
+           verified_token_mismatch=int((tt != ot).sum()), offset_mismatch=int((to != oo).sum()))
+    assert torch.equal(td, od)
+    assert torch.equal(tt, ot)
+    assert torch.equal(to, oo)
