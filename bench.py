@@ -298,6 +298,8 @@ def run_ours(args) -> None:
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6.65 TB/s"},
         "clocks": clock_info,
     }
+    if world == 1 and not args.no_triton:
+        line["triton_b200"] = triton_b200(sets, dev, args.steps, args.warmup, rows_per_s)
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(logits.cpu(), buffers, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)
@@ -305,6 +307,53 @@ def run_ours(args) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+def triton_b200(sets, dev, steps: int, warmup: int, ours_rows_per_s: float) -> dict:
+    """Context, not the reference arm: the reference's own Triton path
+    (`UnshardedFusedSingular.autoregressive`, installed unmodified in baseline/_ref) on this
+    GPU, over the same rotated input sets, captured in CUDA graphs and timed back to back with
+    one event pair, exactly like our steps."""
+    from tests import reference_gpu
+
+    why = reference_gpu.unavailable()
+    if why:
+        return {"unavailable": why}
+    ref = reference_gpu.load()
+    with torch.device(dev):
+        sampler = ref.UnshardedFusedSingular.initialize(VOCAB, batch_size=BATCH)
+    stream = torch.cuda.current_stream(dev)
+    graphs = []
+    for w in sets:
+        b = w["buffers"]
+
+        def step(w=w, b=b):
+            return sampler.autoregressive(w["logits"], b, logprobs=True)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            step()
+        graphs.append(graph)
+    for i in range(max(warmup, INPUT_SETS)):
+        graphs[i % INPUT_SETS].replay()
+    torch.cuda.synchronize()
+    n = max(1, min(steps, 5000))
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    for i in range(n):
+        graphs[i % INPUT_SETS].replay()
+    end.record(stream)
+    torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / n
+    del graphs
+    rows = BATCH / (ms * 1e-3)
+    return {"value": round(rows, 1), "unit": "rows/s", "ms_per_step": round(ms, 6), "steps": n,
+            "ours_over_triton": round(ours_rows_per_s / rows, 3), "block_n": sampler.block_n,
+            "how": "reference UnshardedFusedSingular.autoregressive (Triton, unmodified, baseline/_ref) on the same "
+                   "4 rotated config-2 input sets, CUDA-graph replay, one event pair over the steps"}
 
 
 # ------------------------------------------------------------------------------------------
@@ -556,6 +605,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-triton", action="store_true", help="skip the reference-Triton-on-this-GPU context field")
     ap.add_argument("--workload", choices=["sampling", "populate"], default="sampling",
                     help="sampling: the headline fused-sampling step; populate: batched slot admission")
     args = ap.parse_args()

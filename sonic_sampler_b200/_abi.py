@@ -280,7 +280,8 @@ def load_library(path: os.PathLike | str | None = None) -> ctypes.CDLL:
     global _LIB
     if _LIB is not None and path is None:
         return _LIB
-    target = Path(path) if path is not None else LIB_PATH
+    # SONIC_B200_LIBRARY selects another build of the same ABI (the phase-stamp variant)
+    target = Path(path) if path is not None else Path(os.environ.get("SONIC_B200_LIBRARY", LIB_PATH))
     if not target.is_file():
         raise RuntimeError(
             f"{target} is missing: build the CUDA extension first "

@@ -17,6 +17,8 @@ from pathlib import Path
 PACKAGE_DIR = Path(__file__).resolve().parent
 CSRC = PACKAGE_DIR / "csrc"
 OUT = PACKAGE_DIR / "_lib" / "libsonic_b200.so"
+# diagnostic variant with per-phase timing stamps (python -m sonic_sampler_b200.phases)
+STAMPS_OUT = PACKAGE_DIR / "_lib" / "libsonic_b200_stamps.so"
 SOURCES = [CSRC / "sampler.cu"]
 HEADERS = [CSRC / "common.cuh", CSRC / "exports.map", PACKAGE_DIR.parent / "include" / "sonic_b200.h"]
 
@@ -41,25 +43,28 @@ def nvcc_path() -> str:
     raise RuntimeError("nvcc not found (set CUDA_HOME or put nvcc on PATH)")
 
 
-def stale() -> bool:
-    if not OUT.is_file():
+def stale(out: Path = OUT) -> bool:
+    if not out.is_file():
         return True
-    t = OUT.stat().st_mtime
+    t = out.stat().st_mtime
     return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
 
 
-def build(force: bool = False, verbose: bool = False) -> Path:
-    if not force and not stale():
-        return OUT
-    OUT.parent.mkdir(parents=True, exist_ok=True)
-    tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc_path(), *NVCC_FLAGS, "-o", str(tmp), *map(str, SOURCES)]
+def build(force: bool = False, verbose: bool = False, stamps: bool = False) -> Path:
+    """Build the product library, or with `stamps` the phase-stamp diagnostic variant."""
+    out = STAMPS_OUT if stamps else OUT
+    if not force and not stale(out):
+        return out
+    out.parent.mkdir(parents=True, exist_ok=True)
+    tmp = out.with_suffix(".so.tmp")
+    cmd = [nvcc_path(), *NVCC_FLAGS, *(["-DSONIC_PHASE_STAMPS"] if stamps else []), "-o", str(tmp),
+           *map(str, SOURCES)]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, OUT)
-    return OUT
+    os.replace(tmp, out)
+    return out
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, stamps="--stamps" in sys.argv))

@@ -529,6 +529,73 @@ constexpr float kFiniteFloor = -3.40282346638528859811704183484516925e+38f;  // 
 constexpr int NW = NT / 32;
 constexpr int QCAP = kMaxK + VPT * 32;  // a warp appends at most 256 keys per chunk
 
+// ---------------------------------------------------------------------------------------
+// Phase stamps: a diagnostic build only (-DSONIC_PHASE_STAMPS, `python -m
+// sonic_sampler_b200.phases`). Each CTA of the singular kernels records %globaltimer (ns)
+// at its phase boundaries, and each warp its clock cycles per activity, into a fixed device
+// array that sonic_phase_stamps() copies out. In the product build every hook below is empty
+// and compiles away.
+// ---------------------------------------------------------------------------------------
+
+enum PhaseCta {  // per-CTA %globaltimer stamps
+  PS_ENTRY, PS_PDL, PS_SETUP, PS_FIRST, PS_WARP0_END, PS_ALL_END, PS_FOLD, PS_LIST, PS_TICKET, PS_MERGE,
+  PS_SELECT, PS_SMID, PS_CTA_SLOTS
+};
+enum PhaseWarp {  // per-warp accumulated clock cycles / counts
+  PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_SLOTS
+};
+constexpr int PS_CTAS = 8192;
+
+#ifdef SONIC_PHASE_STAMPS
+struct PhaseStamps {
+  unsigned long long cta[PS_CTAS][PS_CTA_SLOTS];
+  unsigned long long warp[PS_CTAS][NW][PW_SLOTS];
+};
+__device__ PhaseStamps g_phase;
+
+__device__ __forceinline__ unsigned long long gtimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+struct PhaseClock {
+  unsigned long long acc[PW_SLOTS];
+  int cta;
+  __device__ __forceinline__ PhaseClock() : cta((int)(blockIdx.y * gridDim.x + blockIdx.x)) {
+#pragma unroll
+    for (int i = 0; i < PW_SLOTS; ++i) acc[i] = 0;
+  }
+  __device__ __forceinline__ long long now() const { return clock64(); }
+  __device__ __forceinline__ void add(int slot, long long since) { acc[slot] += (unsigned long long)(clock64() - since); }
+  __device__ __forceinline__ void count(int slot, unsigned long long n) { acc[slot] += n; }
+  // one thread of the CTA stamps slot `slot`
+  __device__ __forceinline__ void stamp(int slot, bool who) const {
+    if (who && cta < PS_CTAS) {
+      g_phase.cta[cta][slot] = gtimer();
+      if (slot == PS_ENTRY) {
+        unsigned smid;
+        asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+        g_phase.cta[cta][PS_SMID] = smid;
+      }
+    }
+  }
+  __device__ __forceinline__ void flush(int warp, int lane) {
+    acc[PW_END] = gtimer();
+    if (lane == 0 && cta < PS_CTAS)
+      for (int i = 0; i < PW_SLOTS; ++i) g_phase.warp[cta][warp][i] = acc[i];
+  }
+};
+#else
+struct PhaseClock {
+  __device__ __forceinline__ long long now() const { return 0; }
+  __device__ __forceinline__ void add(int, long long) {}
+  __device__ __forceinline__ void count(int, unsigned long long) {}
+  __device__ __forceinline__ void stamp(int, bool) const {}
+  __device__ __forceinline__ void flush(int, int) {}
+};
+#endif
+
 template <typename K>
 struct WarpTopK {
   K* list;         // shared memory, 128 keys sorted descending
@@ -1031,8 +1098,11 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const SonicSamplingParams& P = a.params;
   const int64_t c0 = (int64_t)split * cols;
   const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
+  PhaseClock pc;
+  pc.stamp(PS_ENTRY, tid == 0);
 
   pdl_wait();
+  pc.stamp(PS_PDL, tid == 0);
 
   // Chunk 0's logits sit at offset 0 of stage 0 in every stage layout: that copy goes out
   // before the row's parameters are loaded (its bytes are expected without an arrival; the
@@ -1139,6 +1209,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     for (int i = 0; i < min(nck, nst); ++i) issue_chunk(i, i);  // barriers set up above
   }
   __syncthreads();
+  pc.stamp(PS_SETUP, tid == 0);
 
   uint32_t* q = st.queue[warp];
   WarpTopK<uint32_t> w;
@@ -1156,9 +1227,12 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
+      const long long ta = pc.now();
       const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
                                    lane, mm);
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
+      pc.add(PW_ABSORB, ta);
+      pc.count(PW_ABSORBS, 1);
     }
   };
 
@@ -1303,16 +1377,20 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       q[pos++] = key;
     }
     w.qn += total;
+    pc.count(PW_PUSHED, (unsigned long long)total);
     return total;
   };
 
   auto process_group = [&](Raw8& raw, int64_t c, int nvalid, int k) {
+    const long long tp = pc.now();
     if (!greedy) wtk_adopt(w, &st.cut, lane);
     if (rc.fast)
       fast_group(raw, c, nvalid);
     else
       exact_group(raw, c, nvalid);
     if (!greedy) absorb_if_full();
+    pc.add(PW_PROCESS, tp);
+    pc.count(PW_GROUPS, 1);
   };
 
   // groups of this warp: g = warp, warp + NW, ...; columns [c0 + g * GROUP, +GROUP)
@@ -1328,7 +1406,12 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
     // columns whose counts are zero and that hold no drafted token (their value needs no
     // penalty), bound 128 distinct keys.
-    if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+    {
+      const long long tw = pc.now();
+      if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+      pc.add(PW_WAIT, tw);
+      pc.stamp(PS_FIRST, tid == 0);
+    }
     const uint4 xq = *reinterpret_cast<const uint4*>(smem_ring + warp * (GROUP * 2) + lane * 16);
     uint32_t y[4] = {xq.x, xq.y, xq.z, xq.w};
     if (brow) {
@@ -1400,7 +1483,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     Raw8 raw;
     const bool staged = k < nchunks;
     if (staged) {
+      const long long tw = pc.now();
       if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+      pc.add(PW_WAIT, tw);
       const unsigned char* sp = smem_ring + stage * stage_bytes;
       const uint4 xq = *reinterpret_cast<const uint4*>(sp + warp * (GROUP * 2) + lane * 16);
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
@@ -1445,6 +1530,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     process_group(raw, c, nv, k);
     if (staged) {
       // this warp has consumed its slice of the stage; the last of the NW warps refills it
+      const long long tr = pc.now();
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
@@ -1457,6 +1543,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
           }
         }
       }
+      pc.add(PW_RELEASE, tr);
       if (++stage == nst) {
         stage = 0;
         phase ^= 1u;
@@ -1465,6 +1552,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
   if (werr) atomicOr(ws.error, 1u);
   pdl_trigger();
+  pc.stamp(PS_WARP0_END, tid == 0);
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   if (greedy) {
@@ -1477,8 +1565,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
   } else {
     if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    pc.flush(warp, lane);
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
+    pc.stamp(PS_FOLD, tid == 0);
     if (warp == 0) {
       // the split holds at least kk finite candidates when list position kk - 1 is taken
       const int jj = (kk - 1) & 3;
@@ -1517,11 +1607,14 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
           asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
       }
       __threadfence();
+      pc.stamp(PS_LIST, lane == 0);
     }
   }
 
   if (MS) return;  // multistep rows: ms_verify_kernel merges the lists after this grid
-  if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
+  const bool last_cta = arrive_last(ws.tickets + r, splits, &st.flag);
+  pc.stamp(PS_TICKET, tid == 0);
+  if (!last_cta) return;
 
   // ---- merge + selection ----
   const uint32_t flags = a.flags;
@@ -1547,6 +1640,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   uint64_t k[4];
   block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
+  pc.stamp(PS_MERGE, tid == 0);
   if (warp != 0) return;
   if (cand_out) {
     // vocab-sharded step 1: the row's 128 best candidates of this shard, global columns
@@ -1559,6 +1653,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     return;
   }
   select_row(a, r, slot, ind, st.mp, k, lane);
+  pc.stamp(PS_SELECT, lane == 0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -3016,6 +3111,25 @@ static sonic_status static_scratch(void** out) {
 }
 
 }  // namespace sonic
+
+#ifdef SONIC_PHASE_STAMPS
+// Diagnostic build only: copy the phase stamps to `host` (at most `bytes`) and, with `clear`,
+// zero them on the device.
+extern "C" sonic_status sonic_phase_stamps(void* host, size_t bytes, int32_t clear) {
+  const size_t n = std::min(bytes, sizeof(PhaseStamps));
+  if (host && n) {
+    const cudaError_t e = cudaMemcpyFromSymbol(host, g_phase, n);
+    if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("phase stamps: ") + cudaGetErrorString(e));
+  }
+  if (clear) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_phase);
+    if (e == cudaSuccess) e = cudaMemset(p, 0, sizeof(PhaseStamps));
+    if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("phase stamps: ") + cudaGetErrorString(e));
+  }
+  return SONIC_OK;
+}
+#endif
 
 extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, void* stream) {
   if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");

@@ -149,9 +149,11 @@ def test_config2_matches_reference(ref, dev, seed):
 def test_config2_mixed_greedy_matches_reference(ref, dev):
     """A third of the rows greedy (with every processor): the reference's greedy tile rule."""
     w = workloads.config2(dev, seed=11)
-    packed = w["buffers"].flags.packed
-    packed[::3, 0] |= 0x40
-    w["buffers"].flags.target_host = [int(v) for v in packed[:, 0].tolist()]
+    b = w["buffers"]
+    ind = b.flags.packed[:, 0].to(I32)
+    ind[::3] |= 0x40
+    b.flags.packed[:, 0] = ind.to(torch.uint16)
+    b.flags.target_host = [int(v) for v in ind.tolist()]
     _config2_case(ref, dev, w, "config2 mixed greedy")
 
 
@@ -160,8 +162,9 @@ def test_config2_top_logprobs_matches_reference(ref, dev):
     w = workloads.config2(dev, seed=12)
     b = w["buffers"]
     b.top_logprobs.fill_(5)
-    b.flags.packed[:, 0] |= 0x400
-    b.flags.target_host = [int(v) for v in b.flags.packed[:, 0].tolist()]
+    ind = b.flags.packed[:, 0].to(I32) | 0x400
+    b.flags.packed[:, 0] = ind.to(torch.uint16)
+    b.flags.target_host = [int(v) for v in ind.tolist()]
     _config2_case(ref, dev, w, "config2 top-5 logprobs")
 
 
@@ -180,8 +183,11 @@ def _multistep_kwargs(b) -> dict:
     )
 
 
-@pytest.mark.parametrize("varlen,q_dtype", [(True, F32), (False, BF16)])
+@pytest.mark.parametrize("varlen,q_dtype", [(True, BF16), (False, BF16)])
 def test_config3_matches_reference(ref, dev, varlen, q_dtype):
+    """Config 3 with bf16 draft probabilities: the reference's verification kernel does not
+    compile with the fp32 ones config 3 specifies (test_reference_rejects_fp32_draft_probabilities);
+    our fp32 path is pinned by the oracle tests instead."""
     from sonic_sampler_b200.interface.functional.multistep import fused_multistep
 
     c = workloads.config3(dev, seed=8, varlen=varlen)
@@ -244,6 +250,38 @@ def test_config3_matches_reference(ref, dev, varlen, q_dtype):
     assert bool(lp_ok.all()) and torch.equal(zt_t, zt_o) and bool(zl_ok.all())
 
 
+def test_reference_rejects_fp32_draft_probabilities(ref, dev):
+    """The reference cannot verify with fp32 draft probabilities on the GPU: under Triton 3.6
+    its `verify_drafted` (ops/verify.py:134-147) multiplies the bf16 uniforms by the fp32
+    probabilities inside an `if`, and Triton refuses the type change when it compiles the
+    kernel. Pinned here so the deviation record stays true."""
+    import triton
+
+    c = workloads.config3(dev, seed=8, varlen=False)
+    b = c["buffers"].to(dev)
+    with pytest.raises(triton.compiler.errors.CompilationError, match="uniform"):
+        ref.fused_multistep(c["logits"], b.flags.target, c["tokens"].clone(), lookahead=c["gamma"],
+                            max_top_logprobs=20, return_logprobs=True, draft_probabilities=c["probabilities"],
+                            block_n=4096, **_multistep_kwargs(b))
+
+
+def test_reference_rejects_int64_d2t(ref, dev):
+    """The reference cannot draft through an int64 d2t table on the GPU: its prologue
+    (ops/prologue.py:382-386) reloads int32 column ids as the table's int64 entries inside an
+    `if`, which Triton 3.6 refuses. Config 4 therefore compares against the reference with the
+    same table as int32, while our side also runs the int64 table."""
+    import triton
+
+    c = workloads.config4(dev, seed=10)
+    b = c["buffers"].to(dev)
+    sm = c["slot_mapping"]
+    with torch.device(dev):
+        drafter = ref.UnshardedFusedSingular.initialize(32000, batch_size=sm.numel(), lookahead=c["gamma"])
+    with pytest.raises(triton.compiler.errors.CompilationError, match="cols"):
+        drafter.drafting(c["draft_logits"][0], b, timestep=0, slot_mapping=sm, d2t_mapping=c["d2t"],
+                         target_vocab=128256)
+
+
 # ----------------------------------------------------------------------------------------
 # config 4: Eagle-3 cross-vocabulary greedy drafting with slot indirection + greedy verification
 # ----------------------------------------------------------------------------------------
@@ -257,8 +295,10 @@ def test_config4_chain_matches_reference(ref, dev):
     active = sm.numel()
     rows = sm.long()
     results = {}
-    for who in ("theirs", "ours"):
+    for who in ("theirs", "ours", "ours_i32"):
         b = c["buffers"].to(dev)
+        # the reference needs the int32 table (test_reference_rejects_int64_d2t); ours runs both
+        d2t = c["d2t"].to(I32) if who != "ours" else c["d2t"]
         if who == "theirs":
             with torch.device(dev):
                 drafter = ref.UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
@@ -283,3 +323,5 @@ def test_config4_chain_matches_reference(ref, dev):
     assert torch.equal(td, od)
     assert torch.equal(tt, ot)
     assert torch.equal(to, oo)
+    for x, y in zip(results["ours"], results["ours_i32"]):
+        assert torch.equal(x, y)
