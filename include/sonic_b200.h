@@ -39,7 +39,7 @@
 extern "C" {
 #endif
 
-#define SONIC_B200_ABI_VERSION 3
+#define SONIC_B200_ABI_VERSION 4
 
 /* Candidate-set width of the two-stage top-k (reference ops/base.py:24, MAX_K). */
 #define SONIC_MAX_K 128
@@ -69,7 +69,19 @@ enum {
   SONIC_FLAG_UPDATE_COUNTS = 1u << 2,  /* update decode counts with the selected tokens */
   SONIC_FLAG_LOGPROBS = 1u << 3,       /* write selected (and top-Z) logprobs */
   SONIC_FLAG_PROBABILITIES = 1u << 4,  /* singular: write candidate probabilities */
-  SONIC_FLAG_PHILOX = 1u << 5          /* counter-based Philox noise instead of the noise buffers */
+  SONIC_FLAG_PHILOX = 1u << 5,         /* counter-based Philox noise instead of the noise buffers */
+  /* Diagnostics, for tests of the error path: every CTA of a ring-streaming kernel first waits
+   * on a barrier that nothing completes, with a short limit, and then takes the same path as a
+   * real bounded-wait timeout (no outputs written, SONIC_DEVICE_ERR_WAIT in the error word). */
+  SONIC_FLAG_DEBUG_STALL_RING = 1u << 15
+};
+
+/* Bits of a workspace's device error word (sonic_workspace_error). */
+enum {
+  /* A bounded wait for a bulk copy into shared memory gave up. The rows (singular, top-k) or
+   * requests (multistep) of the affected CTAs wrote none of their outputs; the staged noise
+   * rows of sonic_indexed_copy that timed out were not stored. */
+  SONIC_DEVICE_ERR_WAIT = 1u << 0
 };
 
 /*
@@ -261,10 +273,20 @@ sonic_status sonic_merge_candidates(const SonicSingularArgs* args, const uint64_
  * Calls whose sonic_fused_singular_workspace_size() exceeds 4 MiB fail with
  * SONIC_ERR_WORKSPACE. The first call on a device looks up the array's device address (with
  * that device current); make that first call before any stream capture. Each call clears
- * the array's tickets with cudaMemsetAsync on `stream` and allocates nothing. All calls
+ * the array's tickets with cudaMemsetAsync on `stream` and allocates nothing; the array's
+ * error word is left for sonic_workspace_error(NULL, ...) to read. All calls
  * share the one array: calls that may overlap on the GPU (other streams, other host threads
  * on the same device) race and must be serialised by the caller. */
 sonic_status sonic_fused_singular_static(const SonicSingularArgs* args, void* stream);
+
+/* Reads the device error word (SONIC_DEVICE_ERR_* bits, 0 when clean) that the kernels of
+ * earlier calls left in `workspace` (the buffer passed as args->workspace to
+ * sonic_fused_singular, sonic_fused_multistep, sonic_bounded_topk or sonic_shard_candidates)
+ * into *error_out, then clears it. With workspace == NULL it reads the library's own word on the
+ * current device, which sonic_fused_singular_static and sonic_indexed_copy write. The word
+ * stays set across calls until read. Synchronises `stream`: do not call it while the stream
+ * is being captured. No counterpart in the reference, which has no device-side error path. */
+sonic_status sonic_workspace_error(void* workspace, uint32_t* error_out, void* stream);
 
 /* Noise staging: for each i < count, row r = indices[i] (i32 or i64, index_dtype); unless
  * indicator[r] has the greedy bit (0x40), copy `cols` elements of `elem_bytes` bytes from

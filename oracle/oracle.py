@@ -45,6 +45,10 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.argtypes = [ctypes.c_float]
             fn.restype = ctypes.c_float
+        lib.oracle_shard_candidates.argtypes = [ctypes.POINTER(SingularArgs), ctypes.c_void_p]
+        lib.oracle_shard_candidates.restype = ctypes.c_int32
+        lib.oracle_merge_candidates.argtypes = [ctypes.POINTER(SingularArgs), ctypes.c_void_p, ctypes.c_int32]
+        lib.oracle_merge_candidates.restype = ctypes.c_int32
         lib.ox_philox_log_exponential.argtypes = [ctypes.c_uint64, ctypes.c_uint64, ctypes.c_int64, ctypes.c_int64]
         lib.ox_philox_log_exponential.restype = ctypes.c_float
         _LIB = lib
@@ -67,6 +71,21 @@ def fused_multistep(args) -> None:
 
 def bounded_topk(args) -> None:
     _run(load().oracle_bounded_topk, args)
+
+
+def shard_candidates(args, keys) -> None:
+    """Vocab-sharded step 1 of one rank: `keys` (contiguous uint64-sized int64 tensor
+    [rows, 128]) receives each row's 128 best keys of this shard, global columns."""
+    status = load().oracle_shard_candidates(ctypes.byref(args), keys.data_ptr())
+    if status != 0:
+        raise RuntimeError(f"oracle returned status {status}")
+
+
+def merge_candidates(args, gathered, world: int) -> None:
+    """Vocab-sharded step 3: merge gathered [world, rows, 128] keys and select."""
+    status = load().oracle_merge_candidates(ctypes.byref(args), gathered.data_ptr(), world)
+    if status != 0:
+        raise RuntimeError(f"oracle returned status {status}")
 
 
 def exp(x: float) -> float:

@@ -415,18 +415,70 @@ static int64_t row_slot(const SonicSamplingParams* P, int64_t r) {
 /* fused singular (interface/functional/singular.py:75-322)                              */
 /* ------------------------------------------------------------------------------------ */
 
+/* Stochastic selection of row r from its sorted top-128 (singular.py:259-358): masking,
+   Gumbel-max over candidate noise, count update, logprobs, top-Z and candidate probabilities.
+   `idx` are the candidates' columns (before d2t). */
+static void select_stochastic(const SonicSingularArgs* a, int64_t r, int64_t slot, uint16_t ind, float* vals,
+                              const int32_t* idx) {
+  const SonicSamplingParams* P = &a->params;
+  const int zcap = a->max_top_logprobs;
+  float ls[MAXK];
+  if (ind & 0x380) cumulative_masking(P, slot, ind, vals, vals[0]);
+  int64_t tok[MAXK];
+  for (int i = 0; i < MAXK; ++i) tok[i] = a->d2t ? load_index(a->d2t, a->d2t_dtype, idx[i]) : idx[i];
+  float diff[MAXK];
+  for (int i = 0; i < MAXK; ++i) {
+    if (a->flags & SONIC_FLAG_PHILOX)
+      diff[i] = vals[i] - ox_philox_log_exponential(a->philox_seed, a->philox_offset, slot, tok[i]);
+    else
+      diff[i] = rbf(vals[i] - bf2f(a->gumbel[slot * a->gumbel_stride + tok[i]]));
+  }
+  int sel = argmax_first(diff, MAXK);
+  int64_t token = tok[sel];
+  if (a->flags & SONIC_FLAG_UPDATE_COUNTS) {
+    int32_t* d = &P->decode_counts[slot * P->counts_stride + token];
+    *d = (a->flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+  }
+  if (a->flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
+    log_softmax128(vals, vals[0], ls);
+    if ((a->flags & SONIC_FLAG_LOGPROBS) && a->logprobs) {
+      store_float(a->logprobs, a->logprobs_dtype, r * a->logprobs_stride, ls[sel]);
+      if (zcap > 0 && (ind & 0x400) && a->top_logprob_values) {
+        int32_t z = P->top_logprobs[slot];
+        if (z > zcap) z = zcap;
+        for (int i = 0; i < z; ++i) {
+          store_float(a->top_logprob_values, a->logprobs_dtype, r * a->top_stride + i, ls[i]);
+          a->top_logprob_tokens[r * a->top_stride + i] = (int32_t)tok[i];
+        }
+      }
+    }
+    if ((a->flags & SONIC_FLAG_PROBABILITIES) && a->probabilities)
+      for (int i = 0; i < MAXK; ++i)
+        store_float(a->probabilities, a->probabilities_dtype, slot * a->probabilities_stride + tok[i],
+                    ox_exp(ls[i]));
+  }
+  a->tokens[r * a->tokens_stride] = (int32_t)token;
+}
+
+static void greedy_update(const SonicSingularArgs* a, int64_t slot, int64_t token) {
+  const SonicSamplingParams* P = &a->params;
+  if (a->flags & SONIC_FLAG_UPDATE_COUNTS) {
+    int32_t* d = &P->decode_counts[slot * P->counts_stride + token];
+    *d = (a->flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
+  }
+}
+
 sonic_status oracle_fused_singular(const SonicSingularArgs* a) {
   const SonicSamplingParams* P = &a->params;
   const int32_t V = a->vocab_size;
   uint64_t* keys = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)V);
   if (!keys) return SONIC_ERR_INVALID_ARGUMENT;
-  const int zcap = a->max_top_logprobs;
   for (int64_t r = 0; r < a->rows; ++r) {
     const int64_t slot = row_slot(P, r);
     const uint16_t ind = P->indicators[slot];
     const uint16_t* x = (const uint16_t*)a->logits + r * a->logits_stride;
     const int32_t* toks = a->drafted_tokens ? a->drafted_tokens + slot * a->drafted_stride : NULL;
-    float vals[MAXK], ls[MAXK];
+    float vals[MAXK];
     int32_t idx[MAXK];
     int64_t token;
     /* singular rows use grammar row `slot` (prologue.py:45 with timesteps = 1) */
@@ -434,49 +486,90 @@ sonic_status oracle_fused_singular(const SonicSingularArgs* a) {
                  toks ? a->lookahead : 0, keys, &token, vals, idx)) {
       /* greedy (singular.py:219-257) */
       if (a->d2t) token = load_index(a->d2t, a->d2t_dtype, token);
-      if (a->flags & SONIC_FLAG_UPDATE_COUNTS) {
-        int32_t* d = &P->decode_counts[slot * P->counts_stride + token];
-        *d = (a->flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
-      }
+      greedy_update(a, slot, token);
       a->tokens[r * a->tokens_stride] = (int32_t)token;
       continue;
     }
-    /* stochastic (singular.py:259-358) */
-    if (ind & 0x380) cumulative_masking(P, slot, ind, vals, vals[0]);
-    int64_t tok[MAXK];
-    for (int i = 0; i < MAXK; ++i) tok[i] = a->d2t ? load_index(a->d2t, a->d2t_dtype, idx[i]) : idx[i];
-    float diff[MAXK];
-    for (int i = 0; i < MAXK; ++i) {
-      if (a->flags & SONIC_FLAG_PHILOX)
-        diff[i] = vals[i] - ox_philox_log_exponential(a->philox_seed, a->philox_offset, slot, tok[i]);
-      else
-        diff[i] = rbf(vals[i] - bf2f(a->gumbel[slot * a->gumbel_stride + tok[i]]));
-    }
-    int sel = argmax_first(diff, MAXK);
-    token = tok[sel];
-    if (a->flags & SONIC_FLAG_UPDATE_COUNTS) {
-      int32_t* d = &P->decode_counts[slot * P->counts_stride + token];
-      *d = (a->flags & SONIC_FLAG_PREFILL) ? 1 : *d + 1;
-    }
-    if (a->flags & (SONIC_FLAG_LOGPROBS | SONIC_FLAG_PROBABILITIES)) {
-      log_softmax128(vals, vals[0], ls);
-      if ((a->flags & SONIC_FLAG_LOGPROBS) && a->logprobs) {
-        store_float(a->logprobs, a->logprobs_dtype, r * a->logprobs_stride, ls[sel]);
-        if (zcap > 0 && (ind & 0x400) && a->top_logprob_values) {
-          int32_t z = P->top_logprobs[slot];
-          if (z > zcap) z = zcap;
-          for (int i = 0; i < z; ++i) {
-            store_float(a->top_logprob_values, a->logprobs_dtype, r * a->top_stride + i, ls[i]);
-            a->top_logprob_tokens[r * a->top_stride + i] = (int32_t)tok[i];
-          }
-        }
+    select_stochastic(a, r, slot, ind, vals, idx);
+  }
+  free(keys);
+  return SONIC_OK;
+}
+
+/* ------------------------------------------------------------------------------------ */
+/* vocab-sharded singular (the sharded stage-2 scaffolding of interface/functional/        */
+/* singular.py:80-84,129-149 and ops/topk/unpack.py:127-247 sharded_top_k, completed)      */
+/* ------------------------------------------------------------------------------------ */
+
+/* Step 1 of one rank: per row, the processed logits of this shard's `vocab_size` columns
+   (aux-buffer columns offset by shard_offset, prologue.py:382), and their 128 best keys
+   (enc16(value) << 32 | ~global column), sorted descending, zero-padded. Greedy rows take the
+   same keys (the merge picks their best). */
+sonic_status oracle_shard_candidates(const SonicSingularArgs* a, uint64_t* out) {
+  const SonicSamplingParams* P = &a->params;
+  const int32_t V = a->vocab_size;
+  uint64_t* keys = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)V);
+  if (!keys) return SONIC_ERR_INVALID_ARGUMENT;
+  for (int64_t r = 0; r < a->rows; ++r) {
+    const int64_t slot = row_slot(P, r);
+    const uint16_t ind = P->indicators[slot];
+    const uint16_t* x = (const uint16_t*)a->logits + r * a->logits_stride;
+    const int32_t* toks = a->drafted_tokens ? a->drafted_tokens + slot * a->drafted_stride : NULL;
+    const int ntok = toks ? a->lookahead : 0;
+    const int processors = (ind & 0x1F) != 0;
+    for (int64_t c = 0; c < V; ++c) {
+      float v = bf2f(x[c]);
+      const int64_t col = c + a->shard_offset;
+      if (processors || (ind & 0x20)) {
+        int32_t extra = 0;
+        if (processors && toks)
+          for (int t = 0; t < ntok; ++t) extra += (toks[t] == col);
+        v = process_logit(P, ind, slot, slot, col, v, extra);
       }
-      if ((a->flags & SONIC_FLAG_PROBABILITIES) && a->probabilities)
-        for (int i = 0; i < MAXK; ++i)
-          store_float(a->probabilities, a->probabilities_dtype, slot * a->probabilities_stride + tok[i],
-                      ox_exp(ls[i]));
+      keys[c] = ((uint64_t)enc16(f2bf(v)) << 32) | (uint64_t)(0xffffffffu - (uint32_t)col);
     }
-    a->tokens[r * a->tokens_stride] = (int32_t)token;
+    uint64_t top[MAXK];
+    const int n = top_keys(keys, V, MAXK, top);
+    for (int i = 0; i < MAXK; ++i) out[r * MAXK + i] = i < n ? top[i] : 0;
+  }
+  free(keys);
+  return SONIC_OK;
+}
+
+/* Step 3, identical on every rank: merge the `world` lists of every row (gathered
+   [world][rows][128]) into the row's top-128 and select as oracle_fused_singular does; a greedy
+   row takes the largest value with the lowest global column (the reference's own sharded
+   greedy decode, ops/singular.py:61-66, mixes up the shard and block indices and is not
+   followed). `a->vocab_size` is the full vocabulary. */
+sonic_status oracle_merge_candidates(const SonicSingularArgs* a, const uint64_t* gathered, int32_t world) {
+  const SonicSamplingParams* P = &a->params;
+  uint64_t* keys = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)world * MAXK);
+  if (!keys) return SONIC_ERR_INVALID_ARGUMENT;
+  for (int64_t r = 0; r < a->rows; ++r) {
+    const int64_t slot = row_slot(P, r);
+    const uint16_t ind = P->indicators[slot];
+    int64_t n = 0;
+    for (int w = 0; w < world; ++w)
+      for (int i = 0; i < MAXK; ++i) {
+        const uint64_t k = gathered[((int64_t)w * a->rows + r) * MAXK + i];
+        if (k) keys[n++] = k;
+      }
+    uint64_t top[MAXK];
+    const int cnt = top_keys(keys, n, MAXK, top);
+    for (int i = cnt; i < MAXK; ++i) top[i] = 0;
+    if (ind & 0x40) {
+      const int64_t token = cnt ? (int64_t)(0xffffffffu - (uint32_t)top[0]) : -1;
+      if (token >= 0) greedy_update(a, slot, token);
+      a->tokens[r * a->tokens_stride] = (int32_t)token;
+      continue;
+    }
+    float vals[MAXK];
+    int32_t idx[MAXK];
+    for (int i = 0; i < MAXK; ++i) {
+      vals[i] = top[i] ? bf2f(dec16((uint32_t)(top[i] >> 32))) : -INFINITY;
+      idx[i] = top[i] ? (int32_t)(0xffffffffu - (uint32_t)top[i]) : 0;
+    }
+    select_stochastic(a, r, slot, ind, vals, idx);
   }
   free(keys);
   return SONIC_OK;

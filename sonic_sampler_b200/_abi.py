@@ -12,7 +12,7 @@ import ctypes
 import os
 from pathlib import Path
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 MAX_K = 128
 MAX_LOOKAHEAD = 15
 
@@ -36,6 +36,11 @@ FLAG_UPDATE_COUNTS = 1 << 2
 FLAG_LOGPROBS = 1 << 3
 FLAG_PROBABILITIES = 1 << 4
 FLAG_PHILOX = 1 << 5
+# diagnostics: every ring wait of the call first runs out (tests of the bounded-wait error path)
+FLAG_DEBUG_STALL_RING = 1 << 15
+
+# bits of a workspace's device error word (sonic_workspace_error)
+DEVICE_ERR_WAIT = 1 << 0
 
 # parts of sonic_populate_slots
 POPULATE_SCALARS = 0x1
@@ -226,6 +231,7 @@ EXPORTED_SYMBOLS = (
     "sonic_fused_multistep",
     "sonic_bounded_topk",
     "sonic_fused_singular_static",
+    "sonic_workspace_error",
     "sonic_shard_candidates",
     "sonic_merge_candidates",
     "sonic_indexed_copy",
@@ -256,6 +262,8 @@ def _declare(lib: ctypes.CDLL) -> ctypes.CDLL:
         fn = getattr(lib, name)
         fn.argtypes = [ctypes.POINTER(argt), _vp]
         fn.restype = _i32
+    lib.sonic_workspace_error.argtypes = [_vp, ctypes.POINTER(ctypes.c_uint32), _vp]
+    lib.sonic_workspace_error.restype = _i32
     lib.sonic_shard_candidates.argtypes = [ctypes.POINTER(SingularArgs), _vp, _vp]
     lib.sonic_shard_candidates.restype = _i32
     lib.sonic_merge_candidates.argtypes = [ctypes.POINTER(SingularArgs), _vp, _i32, _vp]

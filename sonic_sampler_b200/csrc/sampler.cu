@@ -69,7 +69,11 @@ static Plan split_plan(int64_t units, int64_t V, int chunk) {
   return p;
 }
 
-// workspace: [rows][splits][128] u64 sorted candidate keys | [units] u32 tickets | u32 error
+// workspace: [256-byte header: u32 error word at offset 0] | [rows][splits][128] u64 sorted
+// candidate keys | [units] u32 tickets. The error word sits at a fixed offset so that
+// sonic_workspace_error() can read it without the call's shapes.
+constexpr size_t kWsHeader = 256;
+
 struct Workspace {
   uint64_t* cand;
   uint32_t* tickets;
@@ -79,15 +83,20 @@ struct Workspace {
 static size_t workspace_bytes(int64_t rows, int64_t units, int64_t splits) {
   if (units <= 0) return 0;
   const size_t cand = (size_t)rows * splits * kMaxK * sizeof(uint64_t);
-  const size_t tick = ((size_t)units * sizeof(uint32_t) + 4 + 255) / 256 * 256;
-  return cand + tick;
+  const size_t tick = ((size_t)units * sizeof(uint32_t) + 255) / 256 * 256;
+  return kWsHeader + cand + tick;
 }
+
+// The library's own scratch (sonic_fused_singular_static), held by every GPU that loads the
+// library: its first 4 bytes are also the error word of the calls that take no workspace.
+constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 static Workspace carve(void* base, int64_t rows, int64_t units, int64_t splits) {
   Workspace w;
-  w.cand = (uint64_t*)base;
-  w.tickets = (uint32_t*)((char*)base + (size_t)rows * splits * kMaxK * sizeof(uint64_t));
-  w.error = w.tickets + units;
+  w.error = (uint32_t*)base;
+  w.cand = (uint64_t*)((char*)base + kWsHeader);
+  w.tickets = (uint32_t*)((char*)w.cand + (size_t)rows * splits * kMaxK * sizeof(uint64_t));
   return w;
 }
 
@@ -105,6 +114,8 @@ __device__ __forceinline__ int64_t load_index(const void* p, int32_t dtype, int6
 __device__ __forceinline__ uint64_t ldcg64(const uint64_t* p) {
   return (uint64_t)__ldcg(reinterpret_cast<const unsigned long long*>(p));
 }
+
+__device__ __forceinline__ uint32_t ldcg32(const uint32_t* p) { return __ldcg(p); }
 
 __device__ __forceinline__ void stcg64(uint64_t* p, uint64_t v) {
   __stcg(reinterpret_cast<unsigned long long*>(p), (unsigned long long)v);
@@ -169,6 +180,58 @@ __device__ __forceinline__ RowConsts row_consts(const SonicSamplingParams& P, in
   rc.temp_fast = recip_exact_range(rc.temp);
   // The fast path skips the penalties where both counts are zero; that is exact unless a
   // negative frequency / presence penalty turns a -0.0 logit into +0.0.
+  const bool neg_pen = n.dec && (((ind & 0x4) && (f & 0x8000u)) || ((ind & 0x8) && (p & 0x8000u)));
+  const bool temp_ok = !n.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f);
+  rc.fast = !(ind & 0x40) && !neg_pen && temp_ok;
+  rc.decr = rc.fast && (!n.ctx || rc.rep >= 1.0f);
+  return rc;
+}
+
+// Every per-slot scalar a row may read, loaded in one batch: the loads depend on the slot
+// only (a NULL buffer reads as its neutral value), so they share one memory round trip
+// instead of a chain slot -> indicator -> penalties -> masking parameters.
+struct SlotScalars {
+  uint32_t ind;
+  uint16_t rep, freq, pres, temp, top_p, min_p;
+  int32_t top_k, top_logprobs;
+};
+
+__device__ __forceinline__ SlotScalars load_slot_scalars(const SonicSamplingParams& P, int64_t slot) {
+  SlotScalars s;
+  s.ind = P.indicators[slot];
+  s.rep = P.repetition ? P.repetition[slot] : (uint16_t)0x3f80u;
+  s.freq = P.frequency ? P.frequency[slot] : (uint16_t)0;
+  s.pres = P.presence ? P.presence[slot] : (uint16_t)0;
+  s.temp = P.temperature ? P.temperature[slot] : (uint16_t)0x3f80u;
+  s.top_p = P.top_p ? P.top_p[slot] : (uint16_t)0;
+  s.min_p = P.min_p ? P.min_p[slot] : (uint16_t)0;
+  s.top_k = P.top_k ? P.top_k[slot] : 0;
+  s.top_logprobs = P.top_logprobs ? P.top_logprobs[slot] : 0;
+  return s;
+}
+
+// row_consts from preloaded scalars (same result as row_consts(P, slot, s.ind))
+__device__ __forceinline__ RowConsts row_consts(const SonicSamplingParams& P, const SlotScalars& s) {
+  RowConsts rc;
+  const uint32_t ind = s.ind;
+  rc.ind = ind;
+  Needs& n = rc.nd;
+  n.proc = (ind & 0x1F) != 0;
+  n.g = n.proc && P.grammar && (ind & 0x1);
+  n.dec = n.proc && P.decode_counts && (ind & 0xE);
+  n.ctx = n.dec && P.context_counts && (ind & 0x2);
+  n.bias = n.proc && P.bias && (ind & 0x10);
+  n.temp = (ind & 0x20) != 0;
+  rc.rep = (n.ctx && P.repetition) ? bf2f(s.rep) : 1.0f;
+  rc.rrep = __frcp_rn(rc.rep);
+  rc.rep_fast = recip_exact_range(rc.rep);
+  const uint32_t f = (P.frequency && (ind & 0x4)) ? s.freq : 0u;
+  const uint32_t p = (P.presence && (ind & 0x8)) ? s.pres : 0u;
+  rc.freq2 = f | (f << 16);
+  rc.pres2 = p | (p << 16);
+  rc.temp = (P.temperature && n.temp) ? bf2f(s.temp) : 1.0f;
+  rc.rtemp = __frcp_rn(rc.temp);
+  rc.temp_fast = recip_exact_range(rc.temp);
   const bool neg_pen = n.dec && (((ind & 0x4) && (f & 0x8000u)) || ((ind & 0x8) && (p & 0x8000u)));
   const bool temp_ok = !n.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f);
   rc.fast = !(ind & 0x40) && !neg_pen && temp_ok;
@@ -405,18 +468,24 @@ __device__ __forceinline__ uint64_t to_global<uint64_t>(uint64_t k, int64_t c0) 
   return (k & 0xffffffff00000000ull) | (uint64_t)(0xffffffffu - (uint32_t)col);
 }
 
-// Ticket: true in the last CTA of the unit to arrive; that CTA also re-arms the ticket.
-__device__ __forceinline__ bool arrive_last(uint32_t* ticket, int splits, int* flag) {
+// Ticket: true in the last CTA of the unit to arrive; that CTA also re-arms the ticket. A CTA
+// that took the bounded-wait error path arrives with `failed`: the low 16 bits count the
+// arrivals, the high 16 the failed ones, and `*row_failed` tells the last CTA whether any CTA
+// of the unit failed (its outputs are then left unwritten).
+__device__ __forceinline__ bool arrive_last(uint32_t* ticket, int splits, int* flag, bool failed = false,
+                                            bool* row_failed = nullptr) {
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const uint32_t prev = atomicAdd(ticket, 1u);
-    const bool last = prev == (uint32_t)(splits - 1);
+    const uint32_t prev = atomicAdd(ticket, failed ? 0x10001u : 1u);
+    const bool last = (prev & 0xffffu) == (uint32_t)(splits - 1);
     if (last) *ticket = 0;
-    *flag = last;
+    *flag = (last ? 1 : 0) | ((failed || (prev >> 16)) ? 2 : 0);
   }
   __syncthreads();
-  const bool last = *flag != 0;
+  const int f = *flag;
+  if (row_failed) *row_failed = (f & 2) != 0;
+  const bool last = (f & 1) != 0;
   if (last) __threadfence();
   return last;
 }
@@ -458,6 +527,19 @@ __device__ __forceinline__ MaskParams load_mask_params(const SonicSamplingParams
   m.top_p = m.has_p ? P.top_p[slot] : 0;
   m.min_p = m.has_min_p ? P.min_p[slot] : 0;
   m.top_logprobs = P.top_logprobs ? P.top_logprobs[slot] : 0;
+  m.log_min_p = m.has_min_p ? dlog(bf2f(m.min_p)) : 0.0f;
+  return m;
+}
+
+__device__ __forceinline__ MaskParams mask_params(const SonicSamplingParams& P, const SlotScalars& s) {
+  MaskParams m;
+  m.has_k = P.top_k != nullptr;
+  m.has_p = P.top_p != nullptr;
+  m.has_min_p = P.min_p != nullptr;
+  m.top_k = s.top_k;
+  m.top_p = s.top_p;
+  m.min_p = s.min_p;
+  m.top_logprobs = s.top_logprobs;
   m.log_min_p = m.has_min_p ? dlog(bf2f(m.min_p)) : 0.0f;
   return m;
 }
@@ -542,11 +624,11 @@ enum PhaseCta {  // per-CTA %globaltimer stamps
   PS_SELECT, PS_SMID, PS_CTA_SLOTS
 };
 enum PhaseWarp {  // per-warp accumulated clock cycles / counts
-  PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_SLOTS
+  PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_PUSHPATH, PW_LOADS,
+  PW_SLOTS
 };
-constexpr int PS_CTAS = 8192;
-
 #ifdef SONIC_PHASE_STAMPS
+constexpr int PS_CTAS = 8192;
 struct PhaseStamps {
   unsigned long long cta[PS_CTAS][PS_CTA_SLOTS];
   unsigned long long warp[PS_CTAS][NW][PW_SLOTS];
@@ -799,6 +881,28 @@ constexpr int SG_STAGE = CH * 12 + CH / 8;     // 24832
 constexpr int RING_BYTES = STAGES * SG_STAGE;  // the ring's shared memory
 constexpr int MAX_RING_STAGES = 16;            // stages of rows with fewer streams (logits only: 16)
 
+// A ring wait: polls stage barrier `bar` for phase `parity`, and every 32 polls the CTA's
+// abort flag, which a warp sets when one of its waits gave up. Returns false on a timeout
+// (WAIT_LIMIT polls) or an abort; the caller then leaves the streaming loop.
+__device__ __forceinline__ bool ring_wait(uint64_t* bar, uint32_t parity, const int* abort_flag) {
+  for (uint32_t i = 0; i < WAIT_LIMIT; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 31u) == 31u && *reinterpret_cast<const volatile int*>(abort_flag)) return false;
+  }
+  return false;
+}
+
+// The error path of a ring kernel (one thread): wait, bounded, for the last copy issued into
+// every stage, so that no bulk copy lands in shared memory after the CTA has left.
+__device__ __forceinline__ void ring_drain(uint64_t* bars, const int* nissued, int nst) {
+  for (int i = 0; i < nst; ++i)
+    if (nissued[i] > 0) mbar_wait_bounded(&bars[i], (uint32_t)((nissued[i] - 1) & 1), WAIT_LIMIT);
+}
+
+// Diagnostics (SONIC_FLAG_DEBUG_STALL_RING): a wait that runs out. The barrier is initialised
+// with one expected arrival that nothing ever makes, and the wait gives up after a few polls.
+constexpr uint32_t STALL_TEST_LIMIT = 1u << 10;
+
 __device__ __forceinline__ void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -855,6 +959,18 @@ __device__ __noinline__ float greedy_floor(float tv, bool fast, float t, float r
 // exact top-k is needed (and the cut may come from the k-th key), unless top-Z logprobs
 // beyond k or the candidates' probabilities are written. Multistep rows keep 128 (their
 // stage-2 buffers hold all 128 candidates).
+__device__ __forceinline__ int needed_candidates(const SonicSingularArgs& a, const SlotScalars& s, bool ms) {
+  const SonicSamplingParams& P = a.params;
+  const uint32_t ind = s.ind;
+  if (ms || !(ind & 0x80) || !P.top_k || (a.flags & SONIC_FLAG_PROBABILITIES)) return kMaxK;
+  const int32_t k = s.top_k;
+  if (k < 1 || k >= kMaxK) return kMaxK;
+  int z = 0;
+  if ((a.flags & SONIC_FLAG_LOGPROBS) && (ind & 0x400) && a.max_top_logprobs > 0 && P.top_logprobs)
+    z = min(s.top_logprobs, a.max_top_logprobs);
+  return max(k, min(z, kMaxK));
+}
+
 __device__ __forceinline__ int needed_candidates(const SonicSingularArgs& a, uint32_t ind, int64_t slot, bool ms) {
   const SonicSamplingParams& P = a.params;
   if (ms || !(ind & 0x80) || !P.top_k || (a.flags & SONIC_FLAG_PROBABILITIES)) return kMaxK;
@@ -881,6 +997,9 @@ struct RowSmem {
   int32_t toks[SONIC_MAX_LOOKAHEAD + 1];
   uint64_t bars[MAX_RING_STAGES];  // bulk-copy stage filled
   int rel[MAX_RING_STAGES];        // warps done with the stage
+  int nissued[MAX_RING_STAGES];    // chunks issued into the stage (error-path drain)
+  uint64_t stall_bar;              // diagnostics: a barrier nothing completes
+  int abort;                       // a ring wait gave up: every warp leaves the streaming loop
 };
 
 // After an absorb: the warp's new threshold candidates are its own kk-th key value (own) and
@@ -1113,7 +1232,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     for (int i = 0; i < MAX_RING_STAGES; ++i) {
       mbar_init(&st.bars[i], 1);
       st.rel[i] = 0;
+      st.nissued[i] = 0;
     }
+    mbar_init(&st.stall_bar, 1);
     mbar_fence_init();
     mbar_expect_tx_only(&st.bars[0], CH * 2);
     bulk_load(smem_ring, xrow + c0, CH * 2, &st.bars[0]);
@@ -1139,11 +1260,12 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     drain();
     return;
   }
-  const uint32_t ind = P.indicators[slot];
-  const RowConsts rc = row_consts(P, slot, ind);
+  const SlotScalars sc = load_slot_scalars(P, slot);
+  const uint32_t ind = sc.ind;
+  const RowConsts rc = row_consts(P, sc);
   // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
   const bool greedy = (ind & 0x40) != 0 && !cand_out;
-  const int kk = needed_candidates(a, ind, slot, MS);  // exact leading candidates needed
+  const int kk = needed_candidates(a, sc, MS);  // exact leading candidates needed
   const int mm = (kk + NW - 1) / NW;                   // of them per warp (cut rules)
   // drafted tokens counted as decoded: singular counts all `lookahead` drafted tokens of the
   // slot (ops/prologue.py:175-184); multistep step s counts the request's first s
@@ -1183,6 +1305,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     unsigned char* sp = smem_ring + stage * stage_bytes;
     uint64_t* bar = &st.bars[stage];
     const int64_t cc = c0 + (int64_t)i * cw;
+    ++st.nissued[stage];
     if (i == 0) {
       // the first 2048 columns' logits are on their way already
       if (wide) {
@@ -1203,13 +1326,20 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     if (rgrow) bulk_load(sp + sg_g, rgrow + (cc + shard) / 32, CH / 8, bar);
   };
   if (tid == 0) {
-    st.best = 0ull;
-    st.mp = load_mask_params(P, slot);
-    row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
+    st.abort = 0;
     for (int i = 0; i < min(nck, nst); ++i) issue_chunk(i, i);  // barriers set up above
+    st.best = 0ull;
+    st.mp = mask_params(P, sc);
+    row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
   }
   __syncthreads();
   pc.stamp(PS_SETUP, tid == 0);
+  bool werr = false;
+  if ((a.flags & SONIC_FLAG_DEBUG_STALL_RING) && nck > 0) {
+    // diagnostics: a wait that runs out, then the same error path as a real timeout
+    if (!mbar_wait_bounded(&st.stall_bar, 0u, STALL_TEST_LIMIT)) werr = true;
+    if (werr && lane == 0) *reinterpret_cast<volatile int*>(&st.abort) = 1;
+  }
 
   uint32_t* q = st.queue[warp];
   WarpTopK<uint32_t> w;
@@ -1355,6 +1485,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     uint32_t m = ge_mask8(y, w.vmin2) & raw.g;
     if (nvalid < VPT) m &= (1u << max(nvalid, 0)) - 1u;
     if (!__any_sync(kFull, m)) return 0;
+    const long long tpp = pc.now();
     // candidates of the unpenalised test: penalise those with nonzero counts, test again
     if (__any_sync(kFull, counted && m)) {
       const uint32_t late = (counted && m) ? (m & need_bits()) : 0u;
@@ -1378,6 +1509,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
     w.qn += total;
     pc.count(PW_PUSHED, (unsigned long long)total);
+    pc.add(PW_PUSHPATH, tpp);
     return total;
   };
 
@@ -1401,14 +1533,19 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   // chunk k (full 2048-column chunks only) is group k * NW + warp of every warp
   const int nchunks = wide ? 0 : nck;  // chunks of the standard layout
-  bool werr = false;
+  // a ring wait that gave up: this warp leaves the streaming loop, and the abort flag makes
+  // every other warp's next wait give up at once
+  auto give_up = [&]() {
+    werr = true;
+    if (lane == 0) *reinterpret_cast<volatile int*>(&st.abort) = 1;
+  };
   if (MODE == kTma && rc.fast && !greedy && nchunks > 0 && !(INDIRECT && rc.nd.proc)) {
     // Bootstrap the cut before anything is pushed: the lane maxima of the first chunk, over
     // columns whose counts are zero and that hold no drafted token (their value needs no
     // penalty), bound 128 distinct keys.
     {
       const long long tw = pc.now();
-      if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+      if (werr || !ring_wait(&st.bars[0], 0u, &st.abort)) give_up();
       pc.add(PW_WAIT, tw);
       pc.stamp(PS_FIRST, tid == 0);
     }
@@ -1448,8 +1585,11 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   int stage = 0;
   uint32_t phase = 0;
   // wide chunks (greedy rows): groups 2 * NW * k + 2 * warp and the next one
-  for (int k = 0; k < (wide ? nck : 0); ++k) {
-    if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+  for (int k = 0; k < (wide && !werr ? nck : 0); ++k) {
+    if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
+      give_up();
+      break;
+    }
     const unsigned char* sp = smem_ring + stage * stage_bytes + warp * (GROUP * 4) + lane * 16;
     const int g0 = 2 * NW * k + 2 * warp;
 #pragma unroll 1
@@ -1477,15 +1617,19 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
   }
   // the remaining groups: standard ring chunks, then direct loads
-  for (int k = 0, g = (wide ? 2 * NW * nck : 0) + warp; g < ngroups; ++k, g += NW) {
+  for (int k = 0, g = (wide ? 2 * NW * nck : 0) + warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     Raw8 raw;
     const bool staged = k < nchunks;
     if (staged) {
       const long long tw = pc.now();
-      if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+      if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
+        give_up();
+        break;
+      }
       pc.add(PW_WAIT, tw);
+      const long long tl = pc.now();
       const unsigned char* sp = smem_ring + stage * stage_bytes;
       const uint4 xq = *reinterpret_cast<const uint4*>(sp + warp * (GROUP * 2) + lane * 16);
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
@@ -1524,6 +1668,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
         raw.b[0] = u.x; raw.b[1] = u.y; raw.b[2] = u.z; raw.b[3] = u.w;
       }
       if (rgrow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
+      pc.add(PW_LOADS, tl);
     } else {
       load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, c, nv, raw);
     }
@@ -1550,22 +1695,44 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       }
     }
   }
-  if (werr) atomicOr(ws.error, 1u);
   pdl_trigger();
   pc.stamp(PS_WARP0_END, tid == 0);
+
+  // Bounded-wait error path: a CTA whose ring wait gave up writes nothing for its split. It
+  // records the error, lets its issued copies land, and marks its unit's ticket failed, so
+  // that the row (or multistep request) leaves its outputs unwritten.
+  auto fail_split = [&]() {
+    if (tid == 0) {
+      atomicOr(ws.error, (uint32_t)SONIC_DEVICE_ERR_WAIT);
+      ring_drain(st.bars, st.nissued, nst);
+    }
+    if (MS) {
+      if (tid == 0) atomicOr(ws.tickets + req, 1u);
+      return;
+    }
+    arrive_last(ws.tickets + r, splits, &st.flag, true);
+  };
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   if (greedy) {
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
-    __syncthreads();
+    if (__syncthreads_or(werr)) {
+      fail_split();
+      return;
+    }
     if (tid == 0) {
       stcg64(lists + (int64_t)split * kMaxK, st.best);
       __threadfence();
     }
   } else {
+    // (after a failed wait the absorb only reorders shared memory; the CTA then leaves)
     if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
     pc.flush(warp, lane);
+    if (__syncthreads_or(werr)) {
+      fail_split();
+      return;
+    }
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
     pc.stamp(PS_FOLD, tid == 0);
@@ -1612,9 +1779,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
 
   if (MS) return;  // multistep rows: ms_verify_kernel merges the lists after this grid
-  const bool last_cta = arrive_last(ws.tickets + r, splits, &st.flag);
+  bool row_failed = false;
+  const bool last_cta = arrive_last(ws.tickets + r, splits, &st.flag, false, &row_failed);
   pc.stamp(PS_TICKET, tid == 0);
-  if (!last_cta) return;
+  if (!last_cta || row_failed) return;  // a failed split: the row's outputs stay unwritten
 
   // ---- merge + selection ----
   const uint32_t flags = a.flags;
@@ -1716,6 +1884,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   const int nchunks = MODE == kTma ? (int)((c1 - c0) / PCH) : 0;
   auto issue_chunk = [&](int i, int stage) {  // one thread
     uint64_t* bar = &st.bars[stage];
+    ++st.nissued[stage];
     mbar_expect_tx(bar, (uint32_t)PSTAGE);
     bulk_load(smem_ring + stage * PSTAGE, xrow + c0 + (int64_t)i * PCH, PSTAGE, bar);
   };
@@ -1723,7 +1892,9 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     for (int i = 0; i < nst; ++i) {
       mbar_init(&st.bars[i], 1);
       st.rel[i] = 0;
+      st.nissued[i] = 0;
     }
+    mbar_init(&st.stall_bar, 1);
     mbar_fence_init();
     for (int i = 0; i < min(nchunks, nst); ++i) issue_chunk(i, i);
   }
@@ -1736,17 +1907,29 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       for (int i = 0; i < min(nchunks, nst); ++i) mbar_wait_bounded(&st.bars[i], 0u, WAIT_LIMIT);
     return;
   }
-  const uint32_t ind = P.indicators[slot];
-  const RowConsts rc = row_consts(P, slot, ind);
+  const SlotScalars sc = load_slot_scalars(P, slot);
+  const uint32_t ind = sc.ind;
+  const RowConsts rc = row_consts(P, sc);
   const bool greedy = (ind & 0x40) != 0;
-  const int kk = needed_candidates(a, ind, slot, false);  // exact leading candidates needed
-  const int mm = (kk + NW - 1) / NW;                      // of them per warp (cut rules)
+  const int kk = needed_candidates(a, sc, false);  // exact leading candidates needed
+  const int mm = (kk + NW - 1) / NW;               // of them per warp (cut rules)
   if (tid == 0) {
+    st.abort = 0;
     st.best = 0ull;
-    st.mp = load_mask_params(P, slot);
+    st.mp = mask_params(P, sc);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));
   }
   __syncthreads();
+  bool werr = false;
+  if ((a.flags & SONIC_FLAG_DEBUG_STALL_RING) && MODE == kTma && nchunks > 0) {
+    // diagnostics: a wait that runs out, then the same error path as a real timeout
+    if (!mbar_wait_bounded(&st.stall_bar, 0u, STALL_TEST_LIMIT)) werr = true;
+    if (werr && lane == 0) *reinterpret_cast<volatile int*>(&st.abort) = 1;
+  }
+  auto give_up = [&]() {
+    werr = true;
+    if (lane == 0) *reinterpret_cast<volatile int*>(&st.abort) = 1;
+  };
 
   uint32_t* q = st.queue[warp];
   WarpTopK<uint32_t> w;
@@ -1810,10 +1993,9 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   auto gcol = [&](int g) { return c0 + (int64_t)g * PGROUP + (int64_t)PVPT * lane; };
   auto gvalid = [&](int g) { return (int)max((int64_t)0, min((int64_t)PVPT, c1 - gcol(g))); };
   constexpr int DM = MODE == kTma ? kVec : MODE;
-  bool werr = false;
   if (MODE == kTma && rc.fast && !greedy && nchunks > 0) {
     // cut bootstrap from the first chunk's lane maxima (see lane_max_publish)
-    if (!mbar_wait_bounded(&st.bars[0], 0u, WAIT_LIMIT)) werr = true;
+    if (werr || !ring_wait(&st.bars[0], 0u, &st.abort)) give_up();
     const unsigned char* sp = smem_ring + warp * (PGROUP * 2) + lane * 32;
     const uint4 u0 = *reinterpret_cast<const uint4*>(sp), u1 = *reinterpret_cast<const uint4*>(sp + 16);
     const uint32_t x[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
@@ -1839,13 +2021,16 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint32_t lmv = 0xff80ff80u;
   int stage = 0;
   uint32_t phase = 0;
-  for (int k = 0, g = warp; g < ngroups; ++k, g += NW) {
+  for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     uint32_t x[8];
     const bool staged = k < nchunks;
     if (staged) {
-      if (!mbar_wait_bounded(&st.bars[stage], phase, WAIT_LIMIT)) werr = true;
+      if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
+        give_up();
+        break;
+      }
       const unsigned char* sp = smem_ring + stage * PSTAGE + warp * (PGROUP * 2) + lane * 32;
       const uint4 u0 = *reinterpret_cast<const uint4*>(sp), u1 = *reinterpret_cast<const uint4*>(sp + 16);
       x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
@@ -1887,20 +2072,35 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       }
     }
   }
-  if (werr) atomicOr(ws.error, 1u);
   pdl_trigger();
+
+  // bounded-wait error path (see singular_kernel): no outputs for this row
+  auto fail_split = [&]() {
+    if (tid == 0) {
+      atomicOr(ws.error, (uint32_t)SONIC_DEVICE_ERR_WAIT);
+      if (MODE == kTma) ring_drain(st.bars, st.nissued, nst);
+    }
+    arrive_last(ws.tickets + r, splits, &st.flag, true);
+  };
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   if (greedy) {
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
-    __syncthreads();
+    if (__syncthreads_or(werr)) {
+      fail_split();
+      return;
+    }
     if (tid == 0) {
       stcg64(lists + (int64_t)split * kMaxK, st.best);
       __threadfence();
     }
   } else {
     if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    if (__syncthreads_or(werr)) {
+      fail_split();
+      return;
+    }
     uint32_t fin[4];
     block_fold(st.lists, warp, lane, fin);
     if (warp == 0) {
@@ -1938,7 +2138,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   }
 
-  if (!arrive_last(ws.tickets + r, splits, &st.flag)) return;
+  bool row_failed = false;
+  if (!arrive_last(ws.tickets + r, splits, &st.flag, false, &row_failed) || row_failed) return;
 
   if (greedy) {
     if (warp != 0) return;
@@ -2186,6 +2387,12 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   }
   // a request holds 1..gamma+1 rows; anything else is a malformed cu_seqlens
   T = max((int64_t)1, min(T, (int64_t)(G + 1)));
+  // a CTA of this request's rows gave up a bounded wait (singular_kernel's error path): the
+  // request writes no outputs; its mark is cleared for the next call
+  if (ldcg32(ws.tickets + b) != 0) {
+    if (tid == 0) ws.tickets[b] = 0;
+    return;
+  }
   const int64_t slot = load_slot(P, b);
   if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots) || margin < 0 || margin + T > a.total_rows) {
     if (tid == 0) a.offsets[b] = -1;
@@ -2662,7 +2869,7 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
   sa.vocab_size = a->vocab_size;
   sa.block_n = a->block_n;
   sa.shard_offset = a->shard_offset;
-  sa.flags = a->flags & SONIC_FLAG_PDL;
+  sa.flags = a->flags & (SONIC_FLAG_PDL | SONIC_FLAG_DEBUG_STALL_RING);
   sa.logits = a->logits;
   sa.logits_dtype = a->logits_dtype;
   sa.logits_stride = a->logits_stride;
@@ -2766,7 +2973,14 @@ __global__ void __launch_bounds__(32) indexed_copy_kernel(const CopyArgs c, int6
   for (int64_t j = 0; j < min(n, (int64_t)CP_STAGES); ++j) issue(j);
   for (int64_t j = 0; j < n; ++j) {
     const int s = (int)(j % CP_STAGES);
-    mbar_wait_bounded(&bars[s], (uint32_t)((j / CP_STAGES) & 1), WAIT_LIMIT);
+    if (!mbar_wait_bounded(&bars[s], (uint32_t)((j / CP_STAGES) & 1), WAIT_LIMIT)) {
+      // the chunk never landed: store nothing more, record the error in the library's word
+      // (sonic_workspace_error(NULL, ...)), and let the copies in flight land before leaving
+      atomicOr(reinterpret_cast<uint32_t*>(g_static_scratch), (uint32_t)SONIC_DEVICE_ERR_WAIT);
+      for (int64_t jj = j; jj < min(n, j + (int64_t)CP_STAGES); ++jj)
+        mbar_wait_bounded(&bars[jj % CP_STAGES], (uint32_t)((jj / CP_STAGES) & 1), WAIT_LIMIT);
+      break;
+    }
     if ((live >> s) & 1u) {
       bulk_store(dst[s], ring + s * CP_CHUNK, bytes[s]);
       bulk_commit();
@@ -3083,10 +3297,7 @@ sonic_status sonic_populate_slots(const SonicPopulateArgs* a, void* stream) {
 
 namespace sonic {
 
-constexpr size_t kStaticScratchBytes = size_t(4) << 20;  // 4 MiB
 constexpr int kMaxDevices = 64;
-
-static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
 
 // Device address of g_static_scratch on the current device. In host code the array's name
 // is only a host-side stand-in, so the address comes from cudaGetSymbolAddress, once per
@@ -3131,6 +3342,21 @@ extern "C" sonic_status sonic_phase_stamps(void* host, size_t bytes, int32_t cle
 }
 #endif
 
+extern "C" sonic_status sonic_workspace_error(void* workspace, uint32_t* error_out, void* stream) {
+  if (!error_out) return fail(SONIC_ERR_INVALID_ARGUMENT, "error_out must not be NULL");
+  void* base = workspace;
+  if (!base)
+    if (sonic_status s = static_scratch(&base)) return s;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, base, sizeof(v), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && v) e = cudaMemsetAsync(base, 0, sizeof(v), st);
+  if (e != cudaSuccess) return fail(SONIC_ERR_CUDA, std::string("sonic_workspace_error: ") + cudaGetErrorString(e));
+  *error_out = v;
+  return SONIC_OK;
+}
+
 extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, void* stream) {
   if (!a) return fail(SONIC_ERR_INVALID_ARGUMENT, "args must not be NULL");
   if (a->rows == 0) return SONIC_OK;
@@ -3145,7 +3371,8 @@ extern "C" sonic_status sonic_fused_singular_static(const SonicSingularArgs* a, 
                                          "-byte static scratch; use sonic_fused_singular with a workspace");
   void* base = nullptr;
   if (sonic_status s = static_scratch(&base)) return s;
-  // the tickets and the error word start at zero; the candidate lists are written before use
+  // the tickets start at zero (the candidate lists are written before use; the error word at
+  // offset 0 is left set until sonic_workspace_error reads it)
   const Plan p = singular_plan(a->rows, a->vocab_size);
   const Workspace ws = carve(base, a->rows, a->rows, p.splits);
   const size_t off = (size_t)((char*)ws.tickets - (char*)base);

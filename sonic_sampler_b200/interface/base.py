@@ -129,6 +129,15 @@ class TwoStageTiling:
             raise ValueError(f"vocab size must be at least {MAX_K}, got {vocab_size}")
         return dispatch, vocabulary, block_n
 
+    def device_error(self) -> int:
+        """Read and clear the device error word of this object's workspace: 0 when every call
+        since the last read completed, else SONIC_DEVICE_ERR_* bits (a bounded wait gave up and
+        the affected rows wrote no outputs). Synchronises the current stream; an addition of
+        this library (the reference has no device-side error path)."""
+        from sonic_sampler_b200 import ops
+
+        return ops.workspace_error(self.scratchpad)
+
     def tuning(self, size: int, strategy: TopKStrategy | None = None,
                tuning: TwoStageWarpConfig | None = None) -> tuple[TwoStageWarpConfig, TopKStrategy, int]:
         """Same resolution as the reference (interface/base.py:243-276)."""

@@ -173,14 +173,28 @@ def fused_singular(logits: Tensor, indicators: Tensor, process_group=None, **kwa
     if world <= 1:
         ops.launch_singular(args, logits.device)
         return selection
+    dev = logits.device
+    vocab_sharded_exchange(args, logits.size(0), world, int(kwargs.get("shard_size") or logits.size(1)), dev,
+                           extract=lambda a, keys: ops.launch_shard_candidates(a, keys, dev),
+                           merge=lambda a, gathered, w: ops.launch_merge_candidates(a, gathered, w, dev),
+                           process_group=process_group)
+    return selection
+
+
+def vocab_sharded_exchange(args, rows: int, world: int, shard: int, device, extract, merge,
+                           process_group=None) -> None:
+    """The exchange of the vocab-sharded path, identical on every rank: `extract(args, keys)`
+    writes this rank's [rows, 128] candidate keys (global columns), one all-gather over
+    `process_group` collects the `world` lists, and `merge(args, gathered, world)` merges and
+    selects over the whole vocabulary. The product passes the CUDA steps
+    (sonic_shard_candidates / sonic_merge_candidates); the multi-rank CPU tests pass the
+    oracle's restatement of the same steps."""
     import torch.distributed as dist
 
-    rows = logits.size(0)
-    keys = torch.empty(rows, 128, dtype=torch.int64, device=logits.device)
-    ops.launch_shard_candidates(args, keys, logits.device)
-    gathered = torch.empty(world, rows, 128, dtype=torch.int64, device=logits.device)
+    keys = torch.empty(rows, 128, dtype=torch.int64, device=device)
+    extract(args, keys)
+    # rank-major [world * rows, 128] (the layout every backend's all-gather writes)
+    gathered = torch.empty(world * rows, 128, dtype=torch.int64, device=device)
     dist.all_gather_into_tensor(gathered, keys, group=process_group)
-    shard = int(kwargs.get("shard_size") or logits.size(1))
     args.vocab_size = shard * world  # candidates carry global columns below this bound
-    ops.launch_merge_candidates(args, gathered, world, logits.device)
-    return selection
+    merge(args, gathered.view(world, rows, 128), world)

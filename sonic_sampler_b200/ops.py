@@ -348,6 +348,18 @@ def new_workspace(nbytes: int, device: torch.device) -> Tensor:
     return ws
 
 
+def workspace_error(workspace: Tensor | None, device: torch.device | None = None) -> int:
+    """Read and clear the device error word (DEVICE_ERR_* bits) that earlier calls left in
+    `workspace`, or with None the library's own word (static-scratch and noise-staging
+    calls). Synchronises the current stream of `device`."""
+    dev = workspace.device if workspace is not None else (device or torch.device("cuda", torch.cuda.current_device()))
+    lib = _abi.load_library()
+    out = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        _abi.check(lib.sonic_workspace_error(_ptr(workspace), ctypes.byref(out), _stream(dev)), lib)
+    return int(out.value)
+
+
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 

@@ -31,7 +31,8 @@ from sonic_sampler_b200 import build
 
 PS_ENTRY, PS_PDL, PS_SETUP, PS_FIRST, PS_WARP0_END, PS_ALL_END, PS_FOLD, PS_LIST, PS_TICKET, PS_MERGE, PS_SELECT, \
     PS_SMID, PS_CTA_SLOTS = range(13)
-PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_SLOTS = range(9)
+PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_PUSHPATH, PW_LOADS, \
+    PW_SLOTS = range(11)
 PS_CTAS, NW = 8192, 8
 CTA_BYTES = PS_CTAS * PS_CTA_SLOTS * 8
 TOTAL_BYTES = CTA_BYTES + PS_CTAS * NW * PW_SLOTS * 8
@@ -82,8 +83,8 @@ def summarize(cta: np.ndarray, warp: np.ndarray, n_ctas: int, splits: int, clock
     spread = [(e[e > 0].max() - e[e > 0].min()) / 1e3 for e in ends if (e > 0).sum() > 1]
     lines["warp end spread in a CTA"] = _pct(np.array(spread))
     cyc = lambda i: warp[:, :, i].reshape(-1) / clock_mhz  # noqa: E731 (us)
-    act = {"wait": cyc(PW_WAIT), "process": cyc(PW_PROCESS), "absorb": cyc(PW_ABSORB),
-           "release": cyc(PW_RELEASE)}
+    act = {"wait": cyc(PW_WAIT), "stage loads": cyc(PW_LOADS), "process": cyc(PW_PROCESS),
+           "  of which push path": cyc(PW_PUSHPATH), "  of which absorb": cyc(PW_ABSORB), "release": cyc(PW_RELEASE)}
     per_warp = {k: _pct(v) for k, v in act.items()}
     per_warp["absorbs"] = _pct(warp[:, :, PW_ABSORBS].reshape(-1).astype(float))
     per_warp["keys pushed"] = _pct(warp[:, :, PW_PUSHED].reshape(-1).astype(float))
@@ -122,7 +123,8 @@ def main(argv: list[str]) -> None:
         run(i)
     torch.cuda.synchronize()
     splits = None
-    results = []
+    results, raw = [], []
+    save = argv[argv.index("--save") + 1] if "--save" in argv else None
     for i in range(calls):
         _read(lib)  # clears
         flush.fill_(i & 0xFF)
@@ -132,8 +134,12 @@ def main(argv: list[str]) -> None:
         cta, warp = _read(lib)
         n = int((cta[:, PS_ENTRY] > 0).sum())
         results.append(summarize(cta, warp, n, splits, clock_mhz=_clock_mhz()))
-    results.sort(key=lambda r: r["end_us"])
-    med = results[len(results) // 2]
+        raw.append((cta[:n].copy(), warp[:n].copy()))
+    order = sorted(range(calls), key=lambda i: results[i]["end_us"])
+    med = results[order[calls // 2]]
+    if save:
+        c, w = raw[order[calls // 2]]
+        np.savez(save, cta=c, warp=w)
     print(f"{name}: {calls} calls, median call (last selection at {med['end_us']:.2f} us after the first CTA entry)")
     print(f"CTAs per SM (count of SMs): {med['ctas_per_sm']}")
     print(f"{'CTA phase (us from first entry)':34s}   min  median     max")

@@ -259,7 +259,7 @@ def test_reference_rejects_fp32_draft_probabilities(ref, dev):
 
     c = workloads.config3(dev, seed=8, varlen=False)
     b = c["buffers"].to(dev)
-    with pytest.raises(triton.compiler.errors.CompilationError, match="uniform"):
+    with pytest.raises(triton.compiler.errors.CompilationError, match="verify_drafted"):
         ref.fused_multistep(c["logits"], b.flags.target, c["tokens"].clone(), lookahead=c["gamma"],
                             max_top_logprobs=20, return_logprobs=True, draft_probabilities=c["probabilities"],
                             block_n=4096, **_multistep_kwargs(b))
