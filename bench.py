@@ -253,7 +253,13 @@ def run_ours(args) -> None:
     barrier(world)
     e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(es, ee)), world, dev)
     e2e_rows = weak_rows_per_s(world, BATCH, e2e_steps, e2e_ms)
-    del graphs, graph, e2e_graph
+    del graphs, graph, e2e_graph, sets
+
+    # config 5 on every rank: batch rows split evenly (strong scaling), and for N > 1 the
+    # vocab-sharded variant with its one all-gather
+    c5 = run_config5(world, rank, dev, args.steps, args.warmup) if not args.no_config5 else None
+    c5_sharded = run_config5_sharded(world, rank, dev, args.steps, args.warmup) \
+        if (world > 1 and not args.no_config5) else None
 
     if rank != 0:
         if world > 1:
@@ -298,6 +304,10 @@ def run_ours(args) -> None:
                      "peak_source": "MEASURED_PEAKS.json hbm_gbs (of measured)" if peaks else "fallback 6.65 TB/s"},
         "clocks": clock_info,
     }
+    if c5 is not None:
+        line["config5_strong"] = c5
+    if c5_sharded is not None:
+        line["config5_vocab_sharded"] = c5_sharded
     if world == 1 and not args.no_triton:
         line["triton_b200"] = triton_b200(sets, dev, args.steps, args.warmup, rows_per_s)
     if world == 1 and not args.no_cpu_baseline:
@@ -307,6 +317,124 @@ def run_ours(args) -> None:
         import torch.distributed as dist
 
         dist.destroy_process_group()
+
+
+C5_BATCH, C5_VOCAB = 1024, 256000
+C5_MAX_STEPS = 400  # config 5 steps are ~0.3 ms on one GPU: bound the timed region
+
+
+def _c5_kwargs(c) -> dict:
+    return dict(top_k=c["top_k"], top_p=c["top_p"], block_n=4096, philox_seed=c["philox_seed"], philox_offset=17,
+                return_logprobs=True)
+
+
+def run_config5(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    """Config 5 of BASELINE.json, batch-sharded: B = 1024 rows of V = 256000 bf16 logits, top_k 64
+    -> top_p 0.95 -> Gumbel-max with counter-based Philox noise, the rows split evenly over the
+    ranks (1024 / N each; strong scaling: the job is fixed). One step = one fused_singular call
+    per rank (a CUDA-graph replay), device-timed, max over ranks. Inputs (524 MB / N per rank)
+    exceed L2, so no flush is needed."""
+    from sonic_sampler_b200 import roofline, workloads
+    from sonic_sampler_b200.interface.functional.singular import fused_singular
+
+    rows = C5_BATCH // world
+    c = workloads.config5(dev, seed=11 + rank, batch=rows, vocab=C5_VOCAB)
+    kw = _c5_kwargs(c)
+
+    def step():
+        return fused_singular(c["logits"], c["indicators"], **kw)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    n = max(1, min(steps, C5_MAX_STEPS))
+    for _ in range(max(warmup, 3)):
+        graph.replay()
+    stream = torch.cuda.current_stream(dev)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    start.record(stream)
+    for _ in range(n):
+        graph.replay()
+    end.record(stream)
+    barrier(world)
+    ms = max_over_ranks(start.elapsed_time(end), world, dev) / n
+    del graph
+    ind = [int(c["indicators"][0])] * rows
+    alg = roofline.singular_call_bytes(ind, C5_VOCAB, logprobs=True, top_z=0) * world
+    peak = measured_peaks().get("hbm_gbs", 6650.0)
+    return {"value": round(C5_BATCH / (ms * 1e-3), 1), "unit": "rows/s", "scaling": "strong",
+            "rows_per_gpu": rows, "vocab": C5_VOCAB, "ms_per_step": round(ms, 6), "steps": n,
+            "hbm_frac_per_gpu": round(alg / world / (ms * 1e-3) / 1e9 / peak, 4),
+            "workload": "config5: fused_singular B=1024 (split over the ranks) V=256000 bf16, top_k 64 -> top_p 0.95 "
+                        "-> Philox Gumbel-max, logprobs"}
+
+
+def run_config5_sharded(world: int, rank: int, dev, steps: int, warmup: int) -> dict:
+    """Config 5, vocab-sharded over the ranks: every rank holds the columns [r*V/N, (r+1)*V/N) of
+    all 1024 rows, extracts its 128 best candidates per row (sonic_shard_candidates), one
+    all_gather_into_tensor over NCCL exchanges the [1024, 128] int64 keys (1 MiB a rank), and
+    every rank merges and selects identically (sonic_merge_candidates; Philox noise keyed by the
+    global token, so every rank returns the same tokens). The three steps are timed separately
+    with CUDA events on the launching stream (the collective included), max over ranks."""
+    import torch.distributed as dist
+
+    from sonic_sampler_b200 import ops, workloads
+    from sonic_sampler_b200.interface.functional.singular import prepare_singular
+
+    shard = C5_VOCAB // world
+    c = workloads.config5(dev, seed=5, batch=C5_BATCH, vocab=C5_VOCAB)  # the same on every rank
+    local = c["logits"][:, rank * shard:(rank + 1) * shard].contiguous()
+    del c["logits"]
+    sel, a_ext = prepare_singular(local, c["indicators"], world_size=world, local_rank=rank, shard_size=shard,
+                                  **_c5_kwargs(c))
+    a_mrg = type(a_ext).from_buffer_copy(a_ext)
+    a_mrg.vocab_size = shard * world
+    keys = torch.empty(C5_BATCH, 128, dtype=torch.int64, device=dev)
+    gathered = torch.empty(world * C5_BATCH, 128, dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step(ev=None):
+        if ev:
+            ev[0].record(stream)
+        ops.launch_shard_candidates(a_ext, keys, dev)
+        if ev:
+            ev[1].record(stream)
+        dist.all_gather_into_tensor(gathered, keys)
+        if ev:
+            ev[2].record(stream)
+        ops.launch_merge_candidates(a_mrg, gathered.view(world, C5_BATCH, 128), world, dev)
+        if ev:
+            ev[3].record(stream)
+
+    for _ in range(max(warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    n = max(1, min(steps, C5_MAX_STEPS))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+    barrier(world)
+    for i in range(n):
+        step(evs[i])
+    barrier(world)
+    ext = sum(e[0].elapsed_time(e[1]) for e in evs) / n
+    ag = sum(e[1].elapsed_time(e[2]) for e in evs) / n
+    mrg = sum(e[2].elapsed_time(e[3]) for e in evs) / n
+    tot = evs[0][0].elapsed_time(evs[-1][3]) / n
+    ext, ag, mrg, tot = (max_over_ranks(x, world, dev) for x in (ext, ag, mrg, tot))
+    tokens_ok = None
+    if world > 1:  # every rank must return the same tokens
+        t = sel.tokens.view(-1).to(torch.int64)
+        lo, hi = t.clone(), t.clone()
+        dist.all_reduce(lo, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi, op=dist.ReduceOp.MAX)
+        tokens_ok = bool(torch.equal(lo, hi))
+    return {"value": round(C5_BATCH / (tot * 1e-3), 1), "unit": "rows/s", "ms_per_step": round(tot, 6), "steps": n,
+            "extract_ms": round(ext, 6), "all_gather_ms": round(ag, 6), "merge_ms": round(mrg, 6),
+            "keys_bytes_per_rank": C5_BATCH * 128 * 8, "collective": "torch.distributed.all_gather_into_tensor (NCCL)",
+            "columns_per_gpu": shard, "tokens_identical_on_all_ranks": tokens_ok}
 
 
 def triton_b200(sets, dev, steps: int, warmup: int, ours_rows_per_s: float) -> dict:
@@ -606,6 +734,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-triton", action="store_true", help="skip the reference-Triton-on-this-GPU context field")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 strong-scaling and vocab-sharded fields")
     ap.add_argument("--workload", choices=["sampling", "populate"], default="sampling",
                     help="sampling: the headline fused-sampling step; populate: batched slot admission")
     args = ap.parse_args()

@@ -989,6 +989,7 @@ struct RowSmem {
   K queue[NW][QC];
   K lists[NW][kMaxK];
   unsigned long long cut;  // packed CTA cut, see pack_cut
+  int qn[NW];              // keys queued by each warp (singular_kernel: lanes reserve with atomics)
   float v16[NW];           // each warp's m-th kept key value (-inf while it keeps fewer)
   float vlm[NW];           // each warp's m-th largest lane maximum (see lane_max_publish)
   MaskParams mp;           // the slot's masking parameters (selection epilogue)
@@ -1325,6 +1326,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     if (rbrow) bulk_load(sp + sg_b, rbrow + cc + shard, CH * 2, bar);
     if (rgrow) bulk_load(sp + sg_g, rgrow + (cc + shard) / 32, CH / 8, bar);
   };
+  if (tid < NW) st.qn[tid] = 0;
   if (tid == 0) {
     st.abort = 0;
     for (int i = 0; i < min(nck, nst); ++i) issue_chunk(i, i);  // barriers set up above
@@ -1355,11 +1357,21 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   bool tq = rc.fast && rc.nd.temp;  // fast-path queues hold pre-temperature keys
   auto final_of = [&](float v) { return final_value(v, rc); };
 
+  // Queue slots: each lane with candidates reserves its slots with one shared-memory atomic on
+  // the warp's counter (no warp-wide scan or vote); the queue order is immaterial, as absorbs
+  // sort and keep the top of the union. `sync_qn` makes the count warp-uniform again.
+  auto reserve = [&](int np) { return np ? atomicAdd(&st.qn[warp], np) : 0; };
+  auto sync_qn = [&]() {
+    __syncwarp();
+    w.qn = *reinterpret_cast<volatile int*>(&st.qn[warp]);
+  };
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
       const long long ta = pc.now();
       const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
                                    lane, mm);
+      if (lane == 0) st.qn[warp] = 0;
+      __syncwarp();
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
       pc.add(PW_ABSORB, ta);
       pc.count(PW_ABSORBS, 1);
@@ -1433,7 +1445,11 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       key[j] = (enc16(h) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
       if (j < nvalid && bf2f((uint16_t)h) >= thr) m |= 1u << j;
     }
-    wtk_push(w, q, key, m, lane);
+    int pos = reserve(__popc(m));
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+      if ((m >> j) & 1u) q[pos++] = key[j];
+    sync_qn();
   };
 
   // fast path (see vmin_pair): temperature only for candidates, grammar as a mask bit, and
@@ -1484,33 +1500,31 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
     uint32_t m = ge_mask8(y, w.vmin2) & raw.g;
     if (nvalid < VPT) m &= (1u << max(nvalid, 0)) - 1u;
-    if (!__any_sync(kFull, m)) return 0;
-    const long long tpp = pc.now();
-    // candidates of the unpenalised test: penalise those with nonzero counts, test again
-    if (__any_sync(kFull, counted && m)) {
-      const uint32_t late = (counted && m) ? (m & need_bits()) : 0u;
-      if (late) {
-        penalise(x, late);
+    if (m) {
+      const long long tpp = pc.now();
+      // candidates of the unpenalised test: penalise those with nonzero counts, test again
+      if (counted) {
+        const uint32_t late = m & need_bits();
+        if (late) {
+          penalise(x, late);
 #pragma unroll
-        for (int p = 0; p < 4; ++p) y[p] = rc.nd.bias ? bf2_add(x[p], raw.b[p]) : x[p];
-        m &= ge_mask8(y, w.vmin2) | ~late;
+          for (int p = 0; p < 4; ++p) y[p] = rc.nd.bias ? bf2_add(x[p], raw.b[p]) : x[p];
+          m &= ge_mask8(y, w.vmin2) | ~late;
+        }
       }
+      int pos = reserve(__popc(m));
+      const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
+      pc.count(PW_PUSHED, (unsigned long long)__popc(m));
+      while (m) {
+        const int j = __ffs(m) - 1;
+        m &= m - 1;
+        const uint32_t word = select4(y, j >> 1);
+        q[pos++] = (enc16((j & 1) ? (word >> 16) : (word & 0xffffu)) << 16) | (base - (uint32_t)j);
+      }
+      pc.add(PW_PUSHPATH, tpp);
     }
-    int excl;
-    const int total = warp_offsets(__popc(m), lane, excl);
-    int pos = w.qn + excl;
-    const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
-    while (m) {
-      const int j = __ffs(m) - 1;
-      m &= m - 1;
-      const uint32_t word = select4(y, j >> 1);
-      const uint32_t key = (enc16((j & 1) ? (word >> 16) : (word & 0xffffu)) << 16) | (base - (uint32_t)j);
-      q[pos++] = key;
-    }
-    w.qn += total;
-    pc.count(PW_PUSHED, (unsigned long long)total);
-    pc.add(PW_PUSHPATH, tpp);
-    return total;
+    sync_qn();
+    return 0;
   };
 
   auto process_group = [&](Raw8& raw, int64_t c, int nvalid, int k) {
@@ -1728,6 +1742,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   } else {
     // (after a failed wait the absorb only reorders shared memory; the CTA then leaves)
     if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    if (lane == 0) st.qn[warp] = 0;
     pc.flush(warp, lane);
     if (__syncthreads_or(werr)) {
       fail_split();
@@ -1759,6 +1774,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
         absorb_if_full();
       }
       if (w.qn) wtk_absorb(w, q, lane);
+      if (lane == 0) st.qn[warp] = 0;
       block_fold(st.lists, warp, lane, fin);
     }
     if (warp == 0) {

@@ -20,7 +20,10 @@ from pathlib import Path
 
 os.environ["TRITON_INTERPRET"] = "1"
 
-REFERENCE_SRC = Path(os.environ.get("SONIC_REFERENCE_SRC", "/root/reference/src"))
+if "SONIC_REFERENCE_SRC" not in os.environ:
+    raise RuntimeError("set SONIC_REFERENCE_SRC to the reference checkout's src/ directory "
+                       "(the sonic_sampler package of tachyontrails/sonic-sampler)")
+REFERENCE_SRC = Path(os.environ["SONIC_REFERENCE_SRC"])
 sys.path.insert(0, str(Path(__file__).resolve().parent / "_shim"))
 sys.path.insert(0, str(REFERENCE_SRC))
 

@@ -4,8 +4,8 @@ Runs the reference's own Triton kernels (tachyontrails/sonic-sampler, its functi
 `fused_singular` / `fused_multistep` and `UnshardedBoundedTopK`) on the CPU through Triton's
 interpreter (see _reference_harness.py), on small seeded inputs, and saves inputs and
 outputs to tests/golden/*.pt. Needs the reference sources (environment variable
-SONIC_REFERENCE_SRC, defaulting to the reference checkout of the development container);
-the GPU box never runs this file.
+SONIC_REFERENCE_SRC, the reference checkout's src/ directory); the GPU box never runs this
+file.
 
     python tests/golden/make_golden.py            # all cases
     python tests/golden/make_golden.py topk_bf16  # one case

@@ -13,10 +13,11 @@ from sonic_sampler_b200.interface.base import TopKStrategy, TwoStageTiling
 from sonic_sampler_b200.interface.dispatch import DispatchSummary, next_power_of_2
 from sonic_sampler_b200.interface.functional.multistep import resolve_batch_vocab
 
-REFERENCE_TABLES = Path("/root/reference/src/sonic_sampler/resources/dispatch")
+# the reference's tuning tables, from its unmodified install in baseline/_ref (git-ignored)
+REFERENCE_TABLES = Path(__file__).resolve().parents[1] / "baseline" / "_ref" / "sonic_sampler" / "resources" / "dispatch"
 
 
-@pytest.mark.skipif(not REFERENCE_TABLES.is_dir(), reason="reference sources not present")
+@pytest.mark.skipif(not REFERENCE_TABLES.is_dir(), reason="reference not installed in baseline/_ref")
 @pytest.mark.parametrize("arch", [90, 100])
 def test_dispatch_table_matches_reference_toml(arch):
     import tomllib
