@@ -253,7 +253,7 @@ def run_ours(args) -> None:
     barrier(world)
     e2e_ms = max_over_ranks(sum(s.elapsed_time(e) for s, e in zip(es, ee)), world, dev)
     e2e_rows = weak_rows_per_s(world, BATCH, e2e_steps, e2e_ms)
-    del graphs, graph, e2e_graph, sets
+    del graphs, graph, e2e_graph
 
     # config 5 on every rank: batch rows split evenly (strong scaling), and for N > 1 the
     # vocab-sharded variant with its one all-gather
@@ -310,6 +310,7 @@ def run_ours(args) -> None:
         line["config5_vocab_sharded"] = c5_sharded
     if world == 1 and not args.no_triton:
         line["triton_b200"] = triton_b200(sets, dev, args.steps, args.warmup, rows_per_s)
+    del sets
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(logits.cpu(), buffers, budget_s=args.cpu_seconds)
     print(json.dumps(line), flush=True)

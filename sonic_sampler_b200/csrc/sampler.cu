@@ -38,7 +38,7 @@ namespace sonic {
 constexpr int NT = 256;                    // threads per CTA
 constexpr int VPT = 8;                     // consecutive columns per thread per chunk
 constexpr int CH = NT * VPT;               // columns per chunk (single-row kernels)
-constexpr int STAGES = 3;                  // bulk-copy ring depth
+constexpr int STAGES = 4;                  // bulk-copy ring depth (stages of every stream)
 constexpr int TARGET_CTAS = 296;           // 148 SMs x 2 resident CTAs: one wave
 constexpr int MAX_SPLIT_COLS = 65536;      // local column index fits 16 bits
 constexpr int MAX_SPLITS = 32;
@@ -610,6 +610,10 @@ constexpr float kFiniteFloor = -3.40282346638528859811704183484516925e+38f;  // 
 
 constexpr int NW = NT / 32;
 constexpr int QCAP = kMaxK + VPT * 32;  // a warp appends at most 256 keys per chunk
+// singular_kernel's queue: 104 keys plus one group's 256, so that two CTAs with a 4-stage
+// ring fit an SM's shared memory; a warp absorbs once more than SABSORB keys are queued
+constexpr int SQCAP = 360;
+constexpr int SABSORB = SQCAP - VPT * 32;
 
 // ---------------------------------------------------------------------------------------
 // Phase stamps: a diagnostic build only (-DSONIC_PHASE_STAMPS, `python -m
@@ -1210,7 +1214,7 @@ __device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r
 template <int MODE, bool INDIRECT, bool MS>
 __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, uint64_t* cand_out, const MsRows ms) {
-  __shared__ __align__(16) RowSmem<uint32_t> st;
+  __shared__ __align__(16) RowSmem<uint32_t, SQCAP> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
@@ -1366,7 +1370,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     w.qn = *reinterpret_cast<volatile int*>(&st.qn[warp]);
   };
   auto absorb_if_full = [&]() {
-    if (w.qn >= kMaxK) {
+    if (w.qn > SABSORB) {
       const long long ta = pc.now();
       const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
                                    lane, mm);
