@@ -1886,7 +1886,7 @@ __device__ __forceinline__ uint32_t half16(const uint32_t (&x)[8], int j) {
 // fixed costs then overlap more; 3 for one-wave grids, which take a deeper ring instead)
 template <int MODE, int MINB>
 __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
-                                                      Workspace ws, int nst) {
+                                                      Workspace ws, int nst, uint64_t* cand_out) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1930,7 +1930,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   const SlotScalars sc = load_slot_scalars(P, slot);
   const uint32_t ind = sc.ind;
   const RowConsts rc = row_consts(P, sc);
-  const bool greedy = (ind & 0x40) != 0;
+  // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
+  const bool greedy = (ind & 0x40) != 0 && !cand_out;
   const int kk = needed_candidates(a, sc, false);  // exact leading candidates needed
   const int mm = (kk + NW - 1) / NW;               // of them per warp (cut rules)
   if (tid == 0) {
@@ -2151,7 +2152,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       for (int j = 0; j < 4; ++j) {
         const uint64_t key = to_global<uint32_t>(fin[j], c0);
         stcg64(out + 4 * lane + j, key);
-        if (key && !(a.flags & SONIC_FLAG_PHILOX) && (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
+        if (key && !cand_out && a.gumbel && !(a.flags & SONIC_FLAG_PHILOX) &&
+            (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
           asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
       }
       __threadfence();
@@ -2174,6 +2176,17 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint64_t k[4];
   block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
   if (warp != 0) return;
+  if (cand_out) {
+    // vocab-sharded step 1: the row's 128 best candidates of this shard, global columns
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint64_t key = k[j];
+      if (key)
+        key = (key & 0xffffffff00000000ull) | (uint64_t)(0xffffffffu - (uint32_t)(key_column(key) + a.shard_offset));
+      stcg64(cand_out + r * kMaxK + 4 * lane + j, key);
+    }
+    return;
+  }
   select_row(a, r, slot, ind, st.mp, k, lane);
 }
 
@@ -2395,8 +2408,9 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   const SonicSamplingParams& P = a.params;
   const int G = a.lookahead;
 
-  pdl_wait();
-
+  // Everything before pdl_wait reads only the call's inputs (never the rows kernel's candidate
+  // lists or failure marks), so under PDL it overlaps the rows kernel's tail. The rows kernel
+  // waited for every earlier kernel of the stream before it let this grid start.
   int64_t margin, T;
   if (a.cu_seqlens) {
     margin = a.cu_seqlens[b];
@@ -2407,12 +2421,6 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   }
   // a request holds 1..gamma+1 rows; anything else is a malformed cu_seqlens
   T = max((int64_t)1, min(T, (int64_t)(G + 1)));
-  // a CTA of this request's rows gave up a bounded wait (singular_kernel's error path): the
-  // request writes no outputs; its mark is cleared for the next call
-  if (ldcg32(ws.tickets + b) != 0) {
-    if (tid == 0) ws.tickets[b] = 0;
-    return;
-  }
   const int64_t slot = load_slot(P, b);
   if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots) || margin < 0 || margin + T > a.total_rows) {
     if (tid == 0) a.offsets[b] = -1;
@@ -2438,6 +2446,15 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
     }
   }
   __syncthreads();
+
+  pdl_wait();
+  // a CTA of this request's rows gave up a bounded wait (singular_kernel's error path): the
+  // request writes no outputs; its mark is cleared for the next call
+  if (ldcg32(ws.tickets + b) != 0) {
+    __syncthreads();
+    if (tid == 0) ws.tickets[b] = 0;
+    return;
+  }
 
   // ---- per-row merge (warp w handles rows w, w+8, ...) ----
   for (int s = warp; s < T; s += NT / 32) {
@@ -2746,8 +2763,9 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
   const bool ind = a->d2t != nullptr;
   const SonicSamplingParams& P = a->params;
-  if (!cand && !ind && !P.grammar && !P.decode_counts && !P.context_counts && !P.bias) {
-    // no per-column processor anywhere in the call: logits-only streaming kernel
+  if (!ind && !P.grammar && !P.decode_counts && !P.context_counts && !P.bias) {
+    // no per-column processor anywhere in the call: logits-only streaming kernel (also for
+    // the vocab-sharded candidates, `cand`)
     const int pm = xvec ? kTma : kScalar;
     const dim3 pgrid(p.splits, a->rows);
     const bool ppdl = (a->flags & SONIC_FLAG_PDL) != 0;
@@ -2759,9 +2777,9 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     cudaStream_t pst = (cudaStream_t)stream;
     const size_t pring = (size_t)nst * PSTAGE;
     const cudaError_t pe =
-        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst)
-                            : launch(plain_kernel<kTma, 3>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst))
-                   : launch(plain_kernel<kScalar, 3>, pgrid, 0, pst, ppdl, *a, p.splits, p.cols, pl2, ws, 0);
+        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst, cand)
+                            : launch(plain_kernel<kTma, 3>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst, cand))
+                   : launch(plain_kernel<kScalar, 3>, pgrid, 0, pst, ppdl, *a, p.splits, p.cols, pl2, ws, 0, cand);
     return check_launch(pe, what);
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
