@@ -167,24 +167,23 @@ def test_nccl_vocab_shards_match_unsharded(dev):
 
 @pytest.mark.parametrize("world", [2, 4])
 def test_emulated_logits_only_shards_match_unsharded_and_oracle(dev, world):
-    """Logits-only rows (config 5's processing: top-k 64, top-p 0.95, Philox noise; every third
-    row greedy) take the logits-only kernel for the shard candidates. The merged selection
-    equals the unsharded GPU path and the CPU oracle's unsharded selection."""
+    """Logits-only rows (config 5's processing: top-k 64, top-p 0.95, Philox noise) take the
+    logits-only kernel for the shard candidates. The merged selection equals the unsharded GPU
+    path and the CPU oracle's unsharded selection. (Greedy rows are left to the one-tile test
+    above: at V = 256000 the unsharded path's tile tie rule and the sharded lowest-column rule
+    may pick different tied columns.)"""
     from oracle import oracle
     from sonic_sampler_b200.interface.functional.singular import fused_singular, prepare_singular
 
     rows, vocab = 64, 256000
     c = workloads.config5(dev, seed=41, batch=rows, vocab=vocab)
     ind = c["indicators"].to(torch.int32)
-    ind[::3] |= 0x40
     kw = dict(indicators=ind.to(torch.uint16), top_k=c["top_k"], top_p=c["top_p"], philox_seed=c["philox_seed"],
               philox_offset=5, return_logprobs=True, logprobs_dtype=F32, block_n=4096)
     ref = fused_singular(c["logits"], **kw)
     sel = _emulated_sharded(c["logits"], kw, world, vocab // world)
     assert torch.equal(sel.tokens.cpu(), ref.tokens.cpu())
-    stoch = ~(ind.cpu() & 0x40).bool()
-    assert torch.equal(sel.logprobs.selected.cpu()[stoch].view(torch.int32),
-                       ref.logprobs.selected.cpu()[stoch].view(torch.int32))
+    assert torch.equal(sel.logprobs.selected.cpu().view(torch.int32), ref.logprobs.selected.cpu().view(torch.int32))
     hk = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in kw.items()}
     host, args = prepare_singular(c["logits"].cpu(), **hk)
     oracle.fused_singular(args)
