@@ -625,7 +625,7 @@ constexpr int SABSORB = SQCAP - VPT * 32;
 
 enum PhaseCta {  // per-CTA %globaltimer stamps
   PS_ENTRY, PS_PDL, PS_SETUP, PS_FIRST, PS_WARP0_END, PS_ALL_END, PS_FOLD, PS_LIST, PS_TICKET, PS_MERGE,
-  PS_SELECT, PS_SMID, PS_CTA_SLOTS
+  PS_SELECT, PS_SMID, PS_SCALARS, PS_ISSUED, PS_CTA_SLOTS
 };
 enum PhaseWarp {  // per-warp accumulated clock cycles / counts
   PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_PUSHPATH, PW_LOADS,
@@ -1268,6 +1268,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const SlotScalars sc = load_slot_scalars(P, slot);
   const uint32_t ind = sc.ind;
   const RowConsts rc = row_consts(P, sc);
+  pc.stamp(PS_SCALARS, tid == 0);
   // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
   const bool greedy = (ind & 0x40) != 0 && !cand_out;
   const int kk = needed_candidates(a, sc, MS);  // exact leading candidates needed
@@ -1333,7 +1334,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   if (tid < NW) st.qn[tid] = 0;
   if (tid == 0) {
     st.abort = 0;
+    // stage 0's copies first: the stages land roughly in the order they are requested
     for (int i = 0; i < min(nck, nst); ++i) issue_chunk(i, i);  // barriers set up above
+    pc.stamp(PS_ISSUED, true);
     st.best = 0ull;
     st.mp = mask_params(P, sc);
     row_smem_init(st, pack_cut(kFiniteFloor, rc.fast ? vmin_pair(kFiniteFloor, rc) : 0u));

@@ -30,7 +30,7 @@ import numpy as np
 from sonic_sampler_b200 import build
 
 PS_ENTRY, PS_PDL, PS_SETUP, PS_FIRST, PS_WARP0_END, PS_ALL_END, PS_FOLD, PS_LIST, PS_TICKET, PS_MERGE, PS_SELECT, \
-    PS_SMID, PS_CTA_SLOTS = range(13)
+    PS_SMID, PS_SCALARS, PS_ISSUED, PS_CTA_SLOTS = range(15)
 PW_WAIT, PW_PROCESS, PW_ABSORB, PW_ABSORBS, PW_PUSHED, PW_RELEASE, PW_END, PW_GROUPS, PW_PUSHPATH, PW_LOADS, \
     PW_SLOTS = range(11)
 PS_CTAS, NW = 8192, 8
@@ -71,7 +71,8 @@ def summarize(cta: np.ndarray, warp: np.ndarray, n_ctas: int, splits: int, clock
     t0 = cta[:, PS_ENTRY].min()
     rel = lambda col: (cta[:, col][cta[:, col] > 0] - t0) / 1e3  # noqa: E731 (us)
     lines = {}
-    names = {PS_ENTRY: "entry", PS_PDL: "pdl wait done", PS_SETUP: "set-up done", PS_FIRST: "first chunk",
+    names = {PS_ENTRY: "entry", PS_PDL: "pdl wait done", PS_SCALARS: "slot scalars loaded",
+             PS_ISSUED: "first chunks issued", PS_SETUP: "set-up done", PS_FIRST: "first chunk",
              PS_WARP0_END: "warp 0 streamed", PS_FOLD: "fold done", PS_LIST: "list written",
              PS_TICKET: "ticket", PS_MERGE: "row merge (last CTA)", PS_SELECT: "selection (last CTA)"}
     for col, name in names.items():

@@ -210,7 +210,8 @@ def runner(name: str, device):
     """A no-argument callable that runs benchmark config `name` once through the public
     interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep; 4: three
     cross-vocabulary greedy drafting steps and a greedy verification, as one chain;
-    5: fused_singular with Philox noise; 1: UnshardedBoundedTopK)."""
+    5: fused_singular with Philox noise; 1: UnshardedBoundedTopK; indexed_copy: the noise
+    staging of GumbelNoise.stage_weights)."""
     dev = torch.device(device)
     if name == "config1":
         from sonic_sampler_b200.interface import UnshardedBoundedTopK
@@ -266,6 +267,17 @@ def runner(name: str, device):
         kw = dict(indicators=c["indicators"], top_k=c["top_k"], top_p=c["top_p"], block_n=4096,
                   philox_seed=c["philox_seed"], philox_offset=17, return_logprobs=True)
         return lambda: fused_singular(c["logits"], **kw)
+    if name == "indexed_copy":
+        from sonic_sampler_b200.core.buffers import GumbelNoise
+
+        # noise staging after verification: 256 slots x 4 steps x V=128256 bf16 rows, 128 slots
+        # staged (every other one stochastic), 262.7 MB read + written
+        g = _gen(dev, 3)
+        draft = torch.randn(256, 4, 128256, generator=g, device=dev).to(BF16)
+        noise = GumbelNoise(target=torch.zeros_like(draft), draft=draft)
+        indices = torch.randperm(256, generator=torch.Generator().manual_seed(4))[:128].to(I32).to(dev)
+        indicator = torch.zeros(256, dtype=torch.uint16, device=dev)
+        return lambda: noise.stage_weights(indices, indicator)
     raise ValueError(f"unknown workload {name!r}")
 
 
