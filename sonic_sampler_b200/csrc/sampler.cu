@@ -1862,6 +1862,8 @@ constexpr int PSTAGE = PCH * 2;        // bytes per stage
 constexpr int PNST_WAVES = 3;         // ring stages of a multi-wave grid: 24 KB, 4 CTAs an SM
 constexpr int PNST_ONE = 9;           // of a one-wave grid: 72 KB, more bytes in flight a CTA
 constexpr int PQCAP = kMaxK + PGROUP;  // a warp appends at most 512 keys per group
+constexpr int SUBW = 65536;            // sub-split of a logits-only CTA: a 16-bit key index
+constexpr int PLAIN_SLOTS = 148 * 4;   // CTA slots of the multi-wave logits-only kernel (4 an SM)
 
 // 16 logits of one lane, pre-temperature bf16 pairs; `nvalid` columns valid (-inf beyond)
 template <int MODE>
@@ -1891,6 +1893,7 @@ template <int MODE, int MINB>
 __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, int nst, uint64_t* cand_out) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
+  __shared__ __align__(16) uint64_t acc_list[kMaxK];  // the CTA's merged top-128 so far (global keys)
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
@@ -1970,11 +1973,15 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   };
   // queue the keys of the set bits of m (16 columns starting at c)
+  // A CTA may cover more columns than a 16-bit key index reaches: it streams them as
+  // consecutive sub-splits of at most SUBW columns, each with its own warp lists (keys local
+  // to the sub-split's first column `cs`), folded into the CTA list at the sub-split's end.
+  int64_t cs = c0;
   auto push16 = [&](const uint32_t (&y)[8], uint32_t m, int64_t c, bool tempered) {
     int excl;
     const int total = warp_offsets(__popc(m), lane, excl);
     int pos = w.qn + excl;
-    const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
+    const uint32_t base = (uint32_t)(0xffff - (int)(c - cs));
     while (m) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
@@ -2045,7 +2052,34 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint32_t lmv = 0xff80ff80u;
   int stage = 0;
   uint32_t phase = 0;
-  for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW) {
+  // end of sub-split j (block-wide): the warps' final absorbs, the fold, and warp 0 merges the
+  // sub-split's list (global keys) into the CTA list; the warp lists restart empty while the
+  // cut carries over (it still bounds kk keys of the CTA list)
+  auto finish_sub = [&](int j, bool exact) {
+    if (w.qn) wtk_absorb(w, q, lane, exact ? false : tq, rc.temp_fast, rc.temp, rc.rtemp);
+    uint32_t fin[4];
+    block_fold(st.lists, warp, lane, fin);
+    if (warp == 0) {
+      uint64_t cur[4], add[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        add[i] = to_global<uint32_t>(fin[i], cs);
+        cur[i] = j == 0 ? 0ull : acc_list[4 * lane + i];
+      }
+      warp_merge128_desc(cur, add, lane);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc_list[4 * lane + i] = cur[i];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st.lists[warp][4 * lane + i] = 0u;
+    w.qn = 0;
+    __syncthreads();
+  };
+  const int nsub = (int)((c1 - c0 + SUBW - 1) / SUBW);
+  constexpr int KSUB = SUBW / PCH;  // a warp's groups per sub-split (one per chunk)
+  for (int j = 0; j < nsub; ++j) {
+  cs = c0 + (int64_t)j * SUBW;
+  for (int k = j * KSUB, g = warp + j * KSUB * NW; k < (j + 1) * KSUB && g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     uint32_t x[8];
@@ -2096,6 +2130,12 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       }
     }
   }
+  if (__syncthreads_or(werr)) {
+    werr = true;
+    break;
+  }
+  if (!greedy && nsub > 1) finish_sub(j, false);
+  }
   pdl_trigger();
 
   // bounded-wait error path (see singular_kernel): no outputs for this row
@@ -2108,6 +2148,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   };
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
+  // one CTA covers the whole row: no workspace list, no ticket, no merge across CTAs
+  const bool whole_row = splits == 1;
   if (greedy) {
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
@@ -2115,45 +2157,49 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       fail_split();
       return;
     }
-    if (tid == 0) {
+    if (tid == 0 && !whole_row) {
       stcg64(lists + (int64_t)split * kMaxK, st.best);
       __threadfence();
     }
   } else {
-    if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
-    if (__syncthreads_or(werr)) {
+    if (werr) {  // every warp saw the failure at the sub-split barrier
       fail_split();
       return;
     }
-    uint32_t fin[4];
-    block_fold(st.lists, warp, lane, fin);
-    if (warp == 0) {
-      // the split holds at least kk finite candidates when list position kk - 1 is taken
-      const int jj = (kk - 1) & 3;
-      const uint32_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
-      const uint32_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
-      if (lane == 0) st.flag = last != 0;
+    if (nsub == 1) {
+      // a single sub-split: its fold is the CTA list
+      if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+      uint32_t fin[4];
+      block_fold(st.lists, warp, lane, fin);
+      if (warp == 0)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc_list[4 * lane + i] = to_global<uint32_t>(fin[i], cs);
+      __syncthreads();
     }
-    __syncthreads();
-    if (!st.flag) {
-      // fewer than kk finite candidates in this split: redo it keeping -inf logits
+    // the CTA holds at least kk finite candidates when list position kk - 1 is taken
+    if (acc_list[kk - 1] == 0ull) {
+      // fewer than kk finite candidates in the CTA's columns: redo them keeping -inf logits
+      __syncthreads();
       if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
       __syncthreads();
       wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
       tq = false;
-      for (int gg = warp; gg < ngroups; gg += NW) {
-        uint32_t x[8];
-        load_x16<DM>(xrow, gcol(gg), gvalid(gg), x);
-        process16(x, gcol(gg), gvalid(gg), true);
+      for (int j = 0; j < nsub; ++j) {
+        cs = c0 + (int64_t)j * SUBW;
+        const int gend = min(ngroups, (j + 1) * KSUB * NW);
+        for (int gg = warp + j * KSUB * NW; gg < gend; gg += NW) {
+          uint32_t x[8];
+          load_x16<DM>(xrow, gcol(gg), gvalid(gg), x);
+          process16(x, gcol(gg), gvalid(gg), true);
+        }
+        finish_sub(j, true);
       }
-      if (w.qn) wtk_absorb(w, q, lane);
-      block_fold(st.lists, warp, lane, fin);
     }
-    if (warp == 0) {
+    if (warp == 0 && !whole_row) {
       uint64_t* out = lists + (int64_t)split * kMaxK;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint64_t key = to_global<uint32_t>(fin[j], c0);
+        const uint64_t key = acc_list[4 * lane + j];
         stcg64(out + 4 * lane + j, key);
         if (key && !cand_out && a.gumbel && !(a.flags & SONIC_FLAG_PHILOX) &&
             (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
@@ -2163,13 +2209,17 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   }
 
-  bool row_failed = false;
-  if (!arrive_last(ws.tickets + r, splits, &st.flag, false, &row_failed) || row_failed) return;
+  if (!whole_row) {
+    bool row_failed = false;
+    if (!arrive_last(ws.tickets + r, splits, &st.flag, false, &row_failed) || row_failed) return;
+  }
 
   if (greedy) {
     if (warp != 0) return;
     uint64_t b = 0;
-    for (int s = lane; s < splits; s += 32) b = umax(b, ldcg64(lists + (int64_t)s * kMaxK));
+    if (whole_row) b = st.best;
+    else
+      for (int s = lane; s < splits; s += 32) b = umax(b, ldcg64(lists + (int64_t)s * kMaxK));
     b = warp_max_u64(b);
     int64_t token = greedy_col(b, log2bn);
     if (token < 0 || token >= a.vocab_size) token = -1;
@@ -2177,8 +2227,14 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     return;
   }
   uint64_t k[4];
-  block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
-  if (warp != 0) return;
+  if (whole_row) {
+    if (warp != 0) return;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) k[i] = acc_list[4 * lane + i];
+  } else {
+    block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
+    if (warp != 0) return;
+  }
   if (cand_out) {
     // vocab-sharded step 1: the row's 128 best candidates of this shard, global columns
 #pragma unroll
@@ -2779,8 +2835,21 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     const int nst = waves ? PNST_WAVES : PNST_ONE;
     cudaStream_t pst = (cudaStream_t)stream;
     const size_t pring = (size_t)nst * PSTAGE;
+    // Grids of several waves pay every CTA's fixed costs (final absorbs, fold, list, ticket,
+    // merge) once per CTA: they take as few CTAs as keep the SMs' 4 slots busy, a CTA streaming
+    // its columns as sub-splits (down to one CTA per row, which then needs no merge at all).
+    // Never more splits than the workspace was sized for.
+    Plan wp = p;
+    if (waves && pm == kTma) {
+      int64_t sp = std::max<int64_t>(1, std::min<int64_t>(p.splits, PLAIN_SLOTS / std::max<int64_t>(1, a->rows)));
+      int64_t wc = (a->vocab_size + sp - 1) / sp;
+      wc = (wc + PCH - 1) / PCH * PCH;
+      wp.splits = (int)((a->vocab_size + wc - 1) / wc);
+      wp.cols = (int)wc;
+    }
+    const dim3 wgrid(wp.splits, a->rows);
     const cudaError_t pe =
-        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst, cand)
+        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, wgrid, pring, pst, ppdl, *a, wp.splits, wp.cols, pl2, ws, nst, cand)
                             : launch(plain_kernel<kTma, 3>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst, cand))
                    : launch(plain_kernel<kScalar, 3>, pgrid, 0, pst, ppdl, *a, p.splits, p.cols, pl2, ws, 0, cand);
     return check_launch(pe, what);

@@ -661,3 +661,43 @@ def test_greedy_temperature_floor_edges(dev):
     kw["temperature"] = temp.to(dev)
     sel, ref, kw, kh = run_singular(x, block_n=1024, **kw)
     assert_selection_equal(sel, ref, kw, kh)
+
+
+def test_multiwave_logits_only_sub_splits(dev):
+    """Logits-only grids of several waves stream each row in one CTA as sub-splits of 65536
+    columns (V = 200003: four sub-splits, the last ragged). Mixed rows: stochastic with top-k /
+    top-p / temperature and top-Z logprobs, greedy rows (the reference tile rule across
+    sub-splits), and rows with fewer than 128 finite logits spread over the sub-splits (the
+    redo that keeps -inf). Tokens and logprobs match the oracle bit for bit."""
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.singular import fused_singular, prepare_singular
+
+    rows, vocab = 600, 200003
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=77)
+    g = torch.Generator(device=dev).manual_seed(78)
+    sparse = torch.arange(2, rows, 7, device=dev)
+    keep = torch.rand(sparse.numel(), vocab, generator=g, device=dev) < 50.0 / vocab
+    x[sparse] = torch.where(keep, x[sparse], torch.full_like(x[sparse], float("-inf")))
+    ind = torch.full((rows,), int(0x80 | 0x100 | 0x20 | 0x400), dtype=torch.int32)
+    ind[::5] = 0x40 | 0x20  # greedy with temperature
+    params = workloads.config2_params(rows, 79)
+    kw = dict(indicators=ind.to(torch.uint16).to(dev),
+              top_k=torch.tensor([k if k < 128 else 64 for k in params.top_k], dtype=I32, device=dev),
+              top_p=torch.tensor(params.top_p, dtype=BF16, device=dev),
+              temperature=torch.tensor(params.temperature, dtype=BF16, device=dev),
+              top_k_logprobs=torch.full((rows,), 6, dtype=I32, device=dev), max_top_logprobs=6,
+              gumbel_noise=workloads.log_exponential((rows, vocab), dev, 80), block_n=4096,
+              return_logprobs=True, logprobs_dtype=F32)
+    sel = fused_singular(x, **kw)
+    torch.cuda.synchronize()
+    sample = torch.cat([torch.arange(0, rows, 13), sparse[:20].cpu()]).unique()
+    kh = host(kw)
+    kh["slot_mapping"] = sample.to(I32)
+    ref, args = prepare_singular(x[sample.to(dev)].cpu(), **kh)
+    oracle.fused_singular(args)
+    assert torch.equal(sel.tokens[sample].cpu(), ref.tokens)
+    stoch = ~(ind[sample] & 0x40).bool()
+    a, b = sel.logprobs.selected[sample].cpu()[stoch], ref.logprobs.selected[stoch]
+    assert torch.equal(torch.isnan(a), torch.isnan(b))
+    assert torch.equal(bits(a)[~torch.isnan(a)], bits(b)[~torch.isnan(b)])
+    assert torch.equal(sel.logprobs.top_k.tokens[sample].cpu()[stoch], ref.logprobs.top_k.tokens[stoch])
