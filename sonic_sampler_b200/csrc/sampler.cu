@@ -1862,8 +1862,8 @@ constexpr int PSTAGE = PCH * 2;        // bytes per stage
 constexpr int PNST_WAVES = 3;         // ring stages of a multi-wave grid: 24 KB, 4 CTAs an SM
 constexpr int PNST_ONE = 9;           // of a one-wave grid: 72 KB, more bytes in flight a CTA
 constexpr int PQCAP = kMaxK + PGROUP;  // a warp appends at most 512 keys per group
-constexpr int SUBW = 65536;            // sub-split of a logits-only CTA: a 16-bit key index
-constexpr int PLAIN_SLOTS = 148 * 4;   // CTA slots of the multi-wave logits-only kernel (4 an SM)
+constexpr int PLAIN_MAX_COLS = 128 * NW * PGROUP;  // a CTA's columns: 128 groups a warp (16-bit key index)
+constexpr int PLAIN_SLOTS = 148 * 4;                // CTA slots of the multi-wave logits-only kernel (4 an SM)
 
 // 16 logits of one lane, pre-temperature bf16 pairs; `nvalid` columns valid (-inf beyond)
 template <int MODE>
@@ -1893,7 +1893,6 @@ template <int MODE, int MINB>
 __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, int nst, uint64_t* cand_out) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
-  __shared__ __align__(16) uint64_t acc_list[kMaxK];  // the CTA's merged top-128 so far (global keys)
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int split = blockIdx.x;
@@ -1973,15 +1972,16 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   };
   // queue the keys of the set bits of m (16 columns starting at c)
-  // A CTA may cover more columns than a 16-bit key index reaches: it streams them as
-  // consecutive sub-splits of at most SUBW columns, each with its own warp lists (keys local
-  // to the sub-split's first column `cs`), folded into the CTA list at the sub-split's end.
-  int64_t cs = c0;
+  // Warp-local key index: the warp's k-th group (columns c0 + (8k + warp) * 512 + [0, 512))
+  // has local columns k * 512 + [0, 512). It grows with the column inside the warp's share and
+  // fits 16 bits for up to 128 groups a warp (PLAIN_MAX_COLS columns a CTA). Lists of
+  // different warps are merged only as 64-bit keys with global columns (warp_global).
+  auto warp_local = [&](int64_t c) { return (uint32_t)((((c - c0) >> 12) << 9) | ((c - c0) & (PGROUP - 1))); };
   auto push16 = [&](const uint32_t (&y)[8], uint32_t m, int64_t c, bool tempered) {
     int excl;
     const int total = warp_offsets(__popc(m), lane, excl);
     int pos = w.qn + excl;
-    const uint32_t base = (uint32_t)(0xffff - (int)(c - cs));
+    const uint32_t base = 0xffffu - warp_local(c);
     while (m) {
       const int j = __ffs(m) - 1;
       m &= m - 1;
@@ -2052,34 +2052,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint32_t lmv = 0xff80ff80u;
   int stage = 0;
   uint32_t phase = 0;
-  // end of sub-split j (block-wide): the warps' final absorbs, the fold, and warp 0 merges the
-  // sub-split's list (global keys) into the CTA list; the warp lists restart empty while the
-  // cut carries over (it still bounds kk keys of the CTA list)
-  auto finish_sub = [&](int j, bool exact) {
-    if (w.qn) wtk_absorb(w, q, lane, exact ? false : tq, rc.temp_fast, rc.temp, rc.rtemp);
-    uint32_t fin[4];
-    block_fold(st.lists, warp, lane, fin);
-    if (warp == 0) {
-      uint64_t cur[4], add[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        add[i] = to_global<uint32_t>(fin[i], cs);
-        cur[i] = j == 0 ? 0ull : acc_list[4 * lane + i];
-      }
-      warp_merge128_desc(cur, add, lane);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc_list[4 * lane + i] = cur[i];
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) st.lists[warp][4 * lane + i] = 0u;
-    w.qn = 0;
-    __syncthreads();
-  };
-  const int nsub = (int)((c1 - c0 + SUBW - 1) / SUBW);
-  constexpr int KSUB = SUBW / PCH;  // a warp's groups per sub-split (one per chunk)
-  for (int j = 0; j < nsub; ++j) {
-  cs = c0 + (int64_t)j * SUBW;
-  for (int k = j * KSUB, g = warp + j * KSUB * NW; k < (j + 1) * KSUB && g < ngroups && !werr; ++k, g += NW) {
+  for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     uint32_t x[8];
@@ -2101,7 +2074,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       const uint32_t m01 = bf2_max(bf2_max(x[0], x[1]), bf2_max(x[2], x[3]));
       const uint32_t m23 = bf2_max(bf2_max(x[4], x[5]), bf2_max(x[6], x[7]));
       lmv = bf2_max(lmv, bf2_max(m01, m23));
-      if (k == 1 || k == 3 || k == 7) {
+      if (k == 1 || k == 3 || k == 7 || k == 15 || k == 31 || k == 63) {
         const uint32_t lo = lmv & 0xffffu, hi = lmv >> 16;
         const uint32_t h = enc16(lo) >= enc16(hi) ? lo : hi;
         lane_max_publish((h & 0x7fffu) <= 0x7f80u ? enc16(h) << 16 : 0u, st.vlm, warp, lane, final_of, mm);
@@ -2130,12 +2103,6 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       }
     }
   }
-  if (__syncthreads_or(werr)) {
-    werr = true;
-    break;
-  }
-  if (!greedy && nsub > 1) finish_sub(j, false);
-  }
   pdl_trigger();
 
   // bounded-wait error path (see singular_kernel): no outputs for this row
@@ -2162,50 +2129,70 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       __threadfence();
     }
   } else {
-    if (werr) {  // every warp saw the failure at the sub-split barrier
+    // (after a failed wait the absorb only reorders shared memory; the CTA then leaves)
+    if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    if (__syncthreads_or(werr)) {
       fail_split();
       return;
     }
-    if (nsub == 1) {
-      // a single sub-split: its fold is the CTA list
-      if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
-      uint32_t fin[4];
-      block_fold(st.lists, warp, lane, fin);
-      if (warp == 0)
+    // every warp's list as 64-bit keys with global columns, laid out [NW][128] over the
+    // queues (free now), then one fold across the warps
+    uint64_t (*lists64)[kMaxK] = reinterpret_cast<uint64_t (*)[kMaxK]>(&st.queue[0][0]);
+    auto fold_warps = [&](uint64_t (&fin)[4]) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc_list[4 * lane + i] = to_global<uint32_t>(fin[i], cs);
-      __syncthreads();
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t key = st.lists[warp][4 * lane + i];
+        uint64_t gk = 0;
+        if (key) {
+          const uint32_t loc = 0xffffu - (key & 0xffffu);
+          const int64_t col = c0 + ((int64_t)(loc >> 9) << 12) + (int64_t)warp * PGROUP + (loc & (PGROUP - 1));
+          gk = ((uint64_t)(key >> 16) << 32) | (uint64_t)(0xffffffffu - (uint32_t)col);
+        }
+        lists64[warp][4 * lane + i] = gk;
+      }
+      block_fold<uint64_t>(lists64, warp, lane, fin);
+    };
+    uint64_t fin[4];
+    fold_warps(fin);
+    if (warp == 0) {
+      // the CTA holds at least kk finite candidates when list position kk - 1 is taken
+      const int jj = (kk - 1) & 3;
+      const uint64_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
+      const uint64_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
+      if (lane == 0) st.flag = last != 0;
     }
-    // the CTA holds at least kk finite candidates when list position kk - 1 is taken
-    if (acc_list[kk - 1] == 0ull) {
+    __syncthreads();
+    if (!st.flag) {
       // fewer than kk finite candidates in the CTA's columns: redo them keeping -inf logits
-      __syncthreads();
       if (tid == 0) row_smem_init(st, pack_cut(__int_as_float(0xff800000), 0u));
       __syncthreads();
       wtk_init(w, st.lists[warp], __int_as_float(0xff800000), lane);
       tq = false;
-      for (int j = 0; j < nsub; ++j) {
-        cs = c0 + (int64_t)j * SUBW;
-        const int gend = min(ngroups, (j + 1) * KSUB * NW);
-        for (int gg = warp + j * KSUB * NW; gg < gend; gg += NW) {
-          uint32_t x[8];
-          load_x16<DM>(xrow, gcol(gg), gvalid(gg), x);
-          process16(x, gcol(gg), gvalid(gg), true);
-        }
-        finish_sub(j, true);
+      for (int gg = warp; gg < ngroups; gg += NW) {
+        uint32_t x[8];
+        load_x16<DM>(xrow, gcol(gg), gvalid(gg), x);
+        process16(x, gcol(gg), gvalid(gg), true);
       }
+      if (w.qn) wtk_absorb(w, q, lane);
+      __syncthreads();
+      fold_warps(fin);
     }
-    if (warp == 0 && !whole_row) {
-      uint64_t* out = lists + (int64_t)split * kMaxK;
+    if (warp == 0) {
+      if (whole_row) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint64_t key = acc_list[4 * lane + j];
-        stcg64(out + 4 * lane + j, key);
-        if (key && !cand_out && a.gumbel && !(a.flags & SONIC_FLAG_PHILOX) &&
-            (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
+        for (int i = 0; i < 4; ++i) lists64[0][4 * lane + i] = fin[i];
+      } else {
+        uint64_t* out = lists + (int64_t)split * kMaxK;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t key = fin[j];
+          stcg64(out + 4 * lane + j, key);
+          if (key && !cand_out && a.gumbel && !(a.flags & SONIC_FLAG_PHILOX) &&
+              (a.target_vocab <= 0 || key_column(key) < a.target_vocab))
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + key_column(key)));
+        }
+        __threadfence();
       }
-      __threadfence();
     }
   }
 
@@ -2229,8 +2216,9 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint64_t k[4];
   if (whole_row) {
     if (warp != 0) return;
+    const uint64_t (*lists64)[kMaxK] = reinterpret_cast<const uint64_t (*)[kMaxK]>(&st.queue[0][0]);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) k[i] = acc_list[4 * lane + i];
+    for (int i = 0; i < 4; ++i) k[i] = lists64[0][4 * lane + i];
   } else {
     block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
     if (warp != 0) return;
@@ -2836,12 +2824,13 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
     cudaStream_t pst = (cudaStream_t)stream;
     const size_t pring = (size_t)nst * PSTAGE;
     // Grids of several waves pay every CTA's fixed costs (final absorbs, fold, list, ticket,
-    // merge) once per CTA: they take as few CTAs as keep the SMs' 4 slots busy, a CTA streaming
-    // its columns as sub-splits (down to one CTA per row, which then needs no merge at all).
-    // Never more splits than the workspace was sized for.
+    // merge) once per CTA: they take as few CTAs as keep the SMs' 4 slots busy, down to one
+    // CTA per row, which then needs no merge at all (a CTA covers up to PLAIN_MAX_COLS
+    // columns). Never more splits than the workspace was sized for.
     Plan wp = p;
     if (waves && pm == kTma) {
       int64_t sp = std::max<int64_t>(1, std::min<int64_t>(p.splits, PLAIN_SLOTS / std::max<int64_t>(1, a->rows)));
+      sp = std::max<int64_t>(sp, (a->vocab_size + PLAIN_MAX_COLS - 1) / PLAIN_MAX_COLS);
       int64_t wc = (a->vocab_size + sp - 1) / sp;
       wc = (wc + PCH - 1) / PCH * PCH;
       wp.splits = (int)((a->vocab_size + wc - 1) / wc);
