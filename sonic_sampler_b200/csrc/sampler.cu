@@ -1900,8 +1900,11 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   const SonicSamplingParams& P = a.params;
   const int64_t c0 = (int64_t)split * cols;
   const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
+  PhaseClock pc;
+  pc.stamp(PS_ENTRY, tid == 0);
 
   pdl_wait();
+  pc.stamp(PS_PDL, tid == 0);
 
   // The ring's addresses depend on the row alone: its first stages go out before the row's
   // parameters are loaded, so the copies overlap that chain of dependent loads.
@@ -1966,9 +1969,12 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
+      const long long ta = pc.now();
       const float t = absorbed_cut(w, wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp, kk), st.v16, warp,
                                    lane, mm);
       if (t > w.thr) wtk_raise(w, &st.cut, t, rc.fast ? vmin_pair(t, rc) : 0u, lane);
+      pc.add(PW_ABSORB, ta);
+      pc.count(PW_ABSORBS, 1);
     }
   };
   // queue the keys of the set bits of m (16 columns starting at c)
@@ -1978,6 +1984,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   // different warps are merged only as 64-bit keys with global columns (warp_global).
   auto warp_local = [&](int64_t c) { return (uint32_t)((((c - c0) >> 12) << 9) | ((c - c0) & (PGROUP - 1))); };
   auto push16 = [&](const uint32_t (&y)[8], uint32_t m, int64_t c, bool tempered) {
+    const long long tpp = pc.now();
+    pc.count(PW_PUSHED, (unsigned long long)__popc(m));
     int excl;
     const int total = warp_offsets(__popc(m), lane, excl);
     int pos = w.qn + excl;
@@ -1990,8 +1998,11 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       q[pos++] = (enc16(h) << 16) | (base - (uint32_t)j);
     }
     w.qn += total;
+    pc.add(PW_PUSHPATH, tpp);
   };
   auto process16 = [&](const uint32_t (&x)[8], int64_t c, int nvalid, bool exact) {
+    const long long tp = pc.now();
+    pc.count(PW_GROUPS, 1);
     const uint32_t valid = nvalid >= PVPT ? 0xffffu : ((1u << max(nvalid, 0)) - 1u);
     if (greedy) {
 #pragma unroll
@@ -2017,6 +2028,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       if (__any_sync(kFull, m)) push16(x, m, c, rc.nd.temp);
     }
     absorb_if_full();
+    pc.add(PW_PROCESS, tp);
   };
 
   // groups of this warp: g = warp, warp + NW, ...; columns [c0 + g * PGROUP, +PGROUP)
@@ -2058,10 +2070,13 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     uint32_t x[8];
     const bool staged = k < nchunks;
     if (staged) {
+      const long long tw = pc.now();
       if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
         give_up();
         break;
       }
+      pc.add(PW_WAIT, tw);
+      if (k == 0) pc.stamp(PS_FIRST, tid == 0);
       const unsigned char* sp = smem_ring + stage * PSTAGE + warp * (PGROUP * 2) + lane * 32;
       const uint4 u0 = *reinterpret_cast<const uint4*>(sp), u1 = *reinterpret_cast<const uint4*>(sp + 16);
       x[0] = u0.x; x[1] = u0.y; x[2] = u0.z; x[3] = u0.w;
@@ -2085,6 +2100,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
     if (staged) {
       // this warp has consumed its slice of the stage; the last of the NW warps refills it
+      const long long tr = pc.now();
       __syncwarp();
       if (lane == 0) {
         __threadfence_block();
@@ -2097,6 +2113,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
           }
         }
       }
+      pc.add(PW_RELEASE, tr);
       if (++stage == nst) {
         stage = 0;
         phase ^= 1u;
@@ -2104,6 +2121,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   }
   pdl_trigger();
+  pc.stamp(PS_WARP0_END, tid == 0);
 
   // bounded-wait error path (see singular_kernel): no outputs for this row
   auto fail_split = [&]() {
@@ -2131,6 +2149,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   } else {
     // (after a failed wait the absorb only reorders shared memory; the CTA then leaves)
     if (w.qn) wtk_absorb(w, q, lane, tq, rc.temp_fast, rc.temp, rc.rtemp);
+    pc.flush(warp, lane);
     if (__syncthreads_or(werr)) {
       fail_split();
       return;
@@ -2154,6 +2173,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     };
     uint64_t fin[4];
     fold_warps(fin);
+    pc.stamp(PS_FOLD, tid == 0);
     if (warp == 0) {
       // the CTA holds at least kk finite candidates when list position kk - 1 is taken
       const int jj = (kk - 1) & 3;
@@ -2219,6 +2239,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     const uint64_t (*lists64)[kMaxK] = reinterpret_cast<const uint64_t (*)[kMaxK]>(&st.queue[0][0]);
 #pragma unroll
     for (int i = 0; i < 4; ++i) k[i] = lists64[0][4 * lane + i];
+    pc.stamp(PS_MERGE, lane == 0);
   } else {
     block_merge_lists(lists, splits, reinterpret_cast<uint64_t*>(&st.queue[0][0]), warp, lane, k);
     if (warp != 0) return;
@@ -2235,6 +2256,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     return;
   }
   select_row(a, r, slot, ind, st.mp, k, lane);
+  pc.stamp(PS_SELECT, lane == 0);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -2476,6 +2498,8 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   const uint32_t ind = P.indicators[slot];
   const bool greedy = (ind & 0x40) != 0;
   const bool stochastic_q = a.draft_probs && !(ind & 0x800) && !greedy;
+  // per-slot parameters of the masking and the top-Z outputs, loaded with the other inputs
+  const MaskParams mp = load_mask_params(P, slot);
   if (tid < T) {
     const int32_t d = a.drafted_tokens[margin + tid];
     sm.drafted[tid] = d;
@@ -2535,7 +2559,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       }
       const float vmax = __shfl_sync(kFull, v[0], 0);
       float ev[4];
-      if (ind & 0x380) warp_masking(load_mask_params(P, slot), ind, v, vmax, lane, ev);
+      if (ind & 0x380) warp_masking(mp, ind, v, vmax, lane, ev);
       float ls[4];
       warp_log_softmax(v, vmax, ls);
 #pragma unroll
@@ -2638,7 +2662,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
         if (s == accepted) t = psel;
         if (lane == 0) store_float(a.logprobs, a.logprobs_dtype, margin + s, dlog(t));
         if (a.max_top_logprobs > 0 && (ind & 0x400) && a.top_logprob_values && P.top_logprobs) {
-          const int z = min(P.top_logprobs[slot], a.max_top_logprobs);
+          const int z = min(mp.top_logprobs, a.max_top_logprobs);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int i = 4 * lane + j;
