@@ -1888,10 +1888,13 @@ __device__ __forceinline__ uint32_t half16(const uint32_t (&x)[8], int j) {
 }
 
 // MINB: CTAs an SM the registers are budgeted for (4 for grids of several waves, whose CTAs'
-// fixed costs then overlap more; 3 for one-wave grids, which take a deeper ring instead)
-template <int MODE, int MINB>
+// fixed costs then overlap more; 3 for one-wave grids, which take a deeper ring instead).
+// MS: the rows of a multistep call (row r is a step of a request, as in singular_kernel's MS
+// mode): every CTA writes its list (greedy rows: its best key) to the workspace for
+// ms_verify_kernel, with no ticket, merge or selection here.
+template <int MODE, int MINB, bool MS>
 __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
-                                                      Workspace ws, int nst, uint64_t* cand_out) {
+                                                      Workspace ws, int nst, uint64_t* cand_out, const MsRows ms) {
   __shared__ __align__(16) RowSmem<uint32_t, PQCAP> st;
   extern __shared__ __align__(128) unsigned char smem_ring[];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -1927,12 +1930,21 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     for (int i = 0; i < min(nchunks, nst); ++i) issue_chunk(i, i);
   }
 
-  const int64_t slot = load_slot(P, r);
-  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
-    if (split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
-    // the copies already issued land before the CTA leaves
+  auto drain = [&]() {  // leaving early: the copies already issued land before the CTA leaves
     if (MODE == kTma && tid == 0)
       for (int i = 0; i < min(nchunks, nst); ++i) mbar_wait_bounded(&st.bars[i], 0u, WAIT_LIMIT);
+  };
+  // MS: row r is step `step` of multistep request `req`
+  int64_t req = r, margin = 0;
+  int step = 0;
+  if (MS && !ms_row(ms, r, req, step, margin)) {
+    drain();
+    return;
+  }
+  const int64_t slot = load_slot(P, req);
+  if (slot < 0 || (P.num_slots > 0 && slot >= P.num_slots)) {
+    if (!MS && split == 0 && tid == 0) a.tokens[r * a.tokens_stride] = -1;
+    drain();
     return;
   }
   const SlotScalars sc = load_slot_scalars(P, slot);
@@ -1940,7 +1952,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   const RowConsts rc = row_consts(P, sc);
   // vocab-sharded step 1 (cand_out) keeps greedy rows' candidates too: exact path, top-128
   const bool greedy = (ind & 0x40) != 0 && !cand_out;
-  const int kk = needed_candidates(a, sc, false);  // exact leading candidates needed
+  const int kk = needed_candidates(a, sc, MS);  // exact leading candidates needed
   const int mm = (kk + NW - 1) / NW;               // of them per warp (cut rules)
   if (tid == 0) {
     st.abort = 0;
@@ -1966,6 +1978,13 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint64_t best = 0;
   bool tq = rc.fast && rc.nd.temp;  // fast-path queues hold pre-temperature keys
   auto final_of = [&](float v) { return final_value(v, rc); };
+  // Greedy rows: bf16(x / t) is monotone in the logit x for a temperature t in (0, max], so a
+  // column whose logit is below the warp's floor (the smallest bf16 logit whose final value
+  // reaches the warp's best key) has a strictly smaller key. A lane keys its 16 columns
+  // exactly only when one of them is not below the floor (NaN logits always are keyed).
+  const bool gfl = greedy && (!rc.nd.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f));
+  uint32_t gf2 = 0xff80ff80u;  // the floor as a bf16 pair (-inf: every column)
+  uint64_t gbest = 0;          // the warp's best key when the floor was set
 
   auto absorb_if_full = [&]() {
     if (w.qn >= kMaxK) {
@@ -2005,13 +2024,43 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     pc.count(PW_GROUPS, 1);
     const uint32_t valid = nvalid >= PVPT ? 0xffffu : ((1u << max(nvalid, 0)) - 1u);
     if (greedy) {
+      bool pass = true;
+      if (gfl) {
+        uint32_t below = 0xffffffffu;
 #pragma unroll
-      for (int j = 0; j < PVPT; ++j) {
-        if ((valid >> j) & 1u) {
-          const uint32_t h = rc.nd.temp ? (uint32_t)f2bf(final_value(bf2f((uint16_t)half16(x, j)), rc)) : half16(x, j);
-          best = umax(best, greedy_key_bits(h, c + j, log2bn));
+        for (int p = 0; p < 8; ++p)
+          below &= __hlt2_mask(*reinterpret_cast<const __nv_bfloat162*>(&x[p]),
+                               *reinterpret_cast<const __nv_bfloat162*>(&gf2));
+        pass = below != 0xffffffffu;
+      }
+      bool rose = false;
+      if (pass) {
+        pc.count(PW_PUSHED, 1);  // diagnostics: lanes that key their columns
+#pragma unroll
+        for (int j = 0; j < PVPT; ++j) {
+          if ((valid >> j) & 1u) {
+            const uint32_t h =
+                rc.nd.temp ? (uint32_t)f2bf(final_value(bf2f((uint16_t)half16(x, j)), rc)) : half16(x, j);
+            const uint64_t k = greedy_key_bits(h, c + j, log2bn);
+            rose |= k > best;
+            best = umax(best, k);
+          }
         }
       }
+      // raise the warp's floor when its best key rose (a NaN or -inf best leaves it)
+      if (gfl && __any_sync(kFull, rose)) {
+        const uint64_t wb = warp_max_u64(best);
+        if (wb > gbest) {
+          gbest = wb;
+          const uint32_t hb = dec16((uint32_t)(wb >> 48));
+          const float tv = bf2f((uint16_t)hb);
+          if (tv > __int_as_float(0xff800000)) {
+            const uint32_t f = rc.nd.temp ? (uint32_t)f2bf(greedy_floor(tv, rc.temp_fast, rc.temp, rc.rtemp)) : hb;
+            gf2 = f | (f << 16);
+          }
+        }
+      }
+      pc.add(PW_PROCESS, tp);
       return;
     }
     wtk_adopt(w, &st.cut, lane);
@@ -2123,18 +2172,20 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   pdl_trigger();
   pc.stamp(PS_WARP0_END, tid == 0);
 
-  // bounded-wait error path (see singular_kernel): no outputs for this row
+  // bounded-wait error path (see singular_kernel): no outputs for this row (multistep: for
+  // its request, which ms_verify_kernel sees marked)
   auto fail_split = [&]() {
     if (tid == 0) {
       atomicOr(ws.error, (uint32_t)SONIC_DEVICE_ERR_WAIT);
       if (MODE == kTma) ring_drain(st.bars, st.nissued, nst);
+      if (MS) atomicOr(ws.tickets + req, 1u);
     }
-    arrive_last(ws.tickets + r, splits, &st.flag, true);
+    if (!MS) arrive_last(ws.tickets + r, splits, &st.flag, true);
   };
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   // one CTA covers the whole row: no workspace list, no ticket, no merge across CTAs
-  const bool whole_row = splits == 1;
+  const bool whole_row = !MS && splits == 1;
   if (greedy) {
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
@@ -2216,6 +2267,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     }
   }
 
+  if (MS) return;  // multistep rows: ms_verify_kernel merges the lists after this grid
   if (!whole_row) {
     bool row_failed = false;
     if (!arrive_last(ws.tickets + r, splits, &st.flag, false, &row_failed) || row_failed) return;
@@ -2821,6 +2873,46 @@ static sonic_status check_singular(const SonicSingularArgs* a, bool selects) {
   return SONIC_OK;
 }
 
+// Rows with no per-column processor anywhere in the call stream through the logits-only
+// kernel: the rows of a singular call, their vocab-sharded candidates (`cand`), or the rows of a
+// multistep call (`ms`). `used` gets the column splits of the launch (at most p.splits, so
+// the lists fit the workspace carved for p).
+static cudaError_t plain_launch(const SonicSingularArgs& a, const Plan& p, const Workspace& ws, cudaStream_t st,
+                                uint64_t* cand, const MsRows* ms, int& used) {
+  const bool xvec = aligned(a.logits, 16) && (a.logits_stride % 8) == 0;
+  const int pm = xvec ? kTma : kScalar;
+  const bool pdl = (a.flags & SONIC_FLAG_PDL) != 0;
+  const int l2 = ilog2(a.block_n);
+  // a grid of several waves keeps 4 CTAs an SM busy with a 3-stage ring (their fixed costs
+  // overlap); one wave streams longer rows per CTA and takes 3 CTAs with a deeper ring
+  const bool waves = (int64_t)p.splits * a.rows > TARGET_CTAS;
+  const int nst = waves ? PNST_WAVES : PNST_ONE;
+  const size_t ring = (size_t)nst * PSTAGE;
+  // Grids of several waves pay every CTA's fixed costs (final absorbs, fold, list, ticket,
+  // merge) once per CTA: they take as few CTAs as keep the SMs' 4 slots busy, down to one
+  // CTA per row, which then needs no merge at all (a CTA covers up to PLAIN_MAX_COLS
+  // columns). Never more splits than the workspace was sized for.
+  Plan wp = p;
+  if (waves && pm == kTma) {
+    int64_t sp = std::max<int64_t>(1, std::min<int64_t>(p.splits, PLAIN_SLOTS / std::max<int64_t>(1, a.rows)));
+    sp = std::max<int64_t>(sp, (a.vocab_size + PLAIN_MAX_COLS - 1) / PLAIN_MAX_COLS);
+    int64_t wc = (a.vocab_size + sp - 1) / sp;
+    wc = (wc + PCH - 1) / PCH * PCH;
+    wp.splits = (int)((a.vocab_size + wc - 1) / wc);
+    wp.cols = (int)wc;
+  }
+  used = wp.splits;
+  const dim3 grid(wp.splits, a.rows);
+  const MsRows m = ms ? *ms : MsRows{nullptr, nullptr, 0, 0};
+  auto go = [&](auto msc) {
+    constexpr bool M = decltype(msc)::value;
+    if (pm != kTma) return launch(plain_kernel<kScalar, 3, M>, grid, 0, st, pdl, a, wp.splits, wp.cols, l2, ws, 0, cand, m);
+    if (waves) return launch(plain_kernel<kTma, 4, M>, grid, ring, st, pdl, a, wp.splits, wp.cols, l2, ws, nst, cand, m);
+    return launch(plain_kernel<kTma, 3, M>, grid, ring, st, pdl, a, wp.splits, wp.cols, l2, ws, nst, cand, m);
+  };
+  return ms ? go(std::true_type{}) : go(std::false_type{});
+}
+
 // The singular launch; with `cand` the last CTA of a row writes the row's top-128 keys
 // (global columns) there instead of selecting.
 static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, uint64_t* cand, const char* what) {
@@ -2837,35 +2929,8 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   if (!ind && !P.grammar && !P.decode_counts && !P.context_counts && !P.bias) {
     // no per-column processor anywhere in the call: logits-only streaming kernel (also for
     // the vocab-sharded candidates, `cand`)
-    const int pm = xvec ? kTma : kScalar;
-    const dim3 pgrid(p.splits, a->rows);
-    const bool ppdl = (a->flags & SONIC_FLAG_PDL) != 0;
-    const int pl2 = ilog2(a->block_n);
-    // a grid of several waves keeps 4 CTAs an SM busy with a 3-stage ring (their fixed costs
-    // overlap); one wave streams longer rows per CTA and takes 3 CTAs with a deeper ring
-    const bool waves = (int64_t)p.splits * a->rows > TARGET_CTAS;
-    const int nst = waves ? PNST_WAVES : PNST_ONE;
-    cudaStream_t pst = (cudaStream_t)stream;
-    const size_t pring = (size_t)nst * PSTAGE;
-    // Grids of several waves pay every CTA's fixed costs (final absorbs, fold, list, ticket,
-    // merge) once per CTA: they take as few CTAs as keep the SMs' 4 slots busy, down to one
-    // CTA per row, which then needs no merge at all (a CTA covers up to PLAIN_MAX_COLS
-    // columns). Never more splits than the workspace was sized for.
-    Plan wp = p;
-    if (waves && pm == kTma) {
-      int64_t sp = std::max<int64_t>(1, std::min<int64_t>(p.splits, PLAIN_SLOTS / std::max<int64_t>(1, a->rows)));
-      sp = std::max<int64_t>(sp, (a->vocab_size + PLAIN_MAX_COLS - 1) / PLAIN_MAX_COLS);
-      int64_t wc = (a->vocab_size + sp - 1) / sp;
-      wc = (wc + PCH - 1) / PCH * PCH;
-      wp.splits = (int)((a->vocab_size + wc - 1) / wc);
-      wp.cols = (int)wc;
-    }
-    const dim3 wgrid(wp.splits, a->rows);
-    const cudaError_t pe =
-        pm == kTma ? (waves ? launch(plain_kernel<kTma, 4>, wgrid, pring, pst, ppdl, *a, wp.splits, wp.cols, pl2, ws, nst, cand)
-                            : launch(plain_kernel<kTma, 3>, pgrid, pring, pst, ppdl, *a, p.splits, p.cols, pl2, ws, nst, cand))
-                   : launch(plain_kernel<kScalar, 3>, pgrid, 0, pst, ppdl, *a, p.splits, p.cols, pl2, ws, 0, cand);
-    return check_launch(pe, what);
+    int used = 0;
+    return check_launch(plain_launch(*a, p, ws, (cudaStream_t)stream, cand, nullptr, used), what);
   }
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
   // with a d2t table the ring streams the logits only, which xvec already allows
@@ -2999,12 +3064,22 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
   sa.params = a->params;
   sa.tokens = a->tokens;
   const MsRows m{a->cu_seqlens, a->drafted_tokens, a->batch_size, a->lookahead};
-  const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
-  int mode = (xvec && params_vec_ok(a->params, a->shard_offset)) ? kVec : kScalar;
-  if (mode == kVec && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
+  const SonicSamplingParams& P = a->params;
+  if (!P.grammar && !P.decode_counts && !P.context_counts && !P.bias) {
+    // no per-column processor anywhere in the call: the rows stream through the logits-only
+    // kernel, whose column splits the verification then reads
+    int used = 0;
+    if (sonic_status s = check_launch(plain_launch(sa, p, ws, st, nullptr, &m, used), "sonic_fused_multistep (rows)"))
+      return s;
+    return check_launch(launch(ms_verify_kernel, dim3(a->batch_size), 0, st, pdl, *a, used, l2, ws),
+                        "sonic_fused_multistep");
+  }
+  const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
+  int mode = (xvec && params_vec_ok(a->params, a->shard_offset)) ? kVec : kScalar;
+  if (mode == kVec && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
   const dim3 grid(p.splits, (unsigned)rows);
   cudaError_t e;
   if (mode == kTma)

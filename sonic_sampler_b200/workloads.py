@@ -192,6 +192,20 @@ def config4(device, seed: int = 0, active: int = 128, slots: int = 256, gamma: i
                 buffers=buffers, gamma=gamma)
 
 
+def config4_chain(c: dict, drafter, verifier, tokens: torch.Tensor):
+    """One config-4 chain: `gamma` greedy drafting steps, each writing its token in place into
+    column t of the per-request table `tokens` (reference interface/singular.py:41-55 with
+    in_place=True), then the verification, which reads the drafted tokens from that table and
+    overwrites it with its outputs. Five launches, no glue between them. (A drafting step reads
+    the drafted tokens per slot, for repetition penalties only; config 4 sets none, so a
+    per-request table serves both calls.)"""
+    b, d2t, sm = c["buffers"], c["d2t"], c["slot_mapping"]
+    for t in range(c["gamma"]):
+        drafter.drafting(c["draft_logits"][t], b, timestep=t, tokens=tokens, in_place=True, slot_mapping=sm,
+                         d2t_mapping=d2t, target_vocab=128256)
+    return verifier(c["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
+
+
 def config5(device, seed: int = 0, batch: int = 1024, vocab: int = 256000):
     """B=1024, V=256000: top_k=64 -> top_p=0.95 -> Gumbel-max with counter-based Philox (seed 1234)."""
     dev = torch.device(device)
@@ -242,24 +256,11 @@ def runner(name: str, device):
         from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
 
         c = config4(dev, seed=10)
-        b, gamma, d2t, sm = c["buffers"], c["gamma"], c["d2t"], c["slot_mapping"]
-        active = sm.numel()
+        active, gamma = c["slot_mapping"].numel(), c["gamma"]
         drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
         verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
         tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
-        # drafted tokens per slot for the drafter, gathered per request for the verifier
-        slot_tokens = torch.zeros(b.top_k.numel(), gamma + 1, dtype=I32, device=dev)
-        rows = sm.long()
-
-        def chain():
-            for t in range(gamma):
-                sel = drafter.drafting(c["draft_logits"][t], b, timestep=t, tokens=slot_tokens if t else None,
-                                       slot_mapping=sm, d2t_mapping=d2t, target_vocab=128256)
-                slot_tokens[rows, t] = sel.tokens[:, 0]
-            tokens.copy_(slot_tokens[rows])
-            return verifier(c["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
-
-        return chain
+        return lambda: config4_chain(c, drafter, verifier, tokens)
     if name == "config5":
         from sonic_sampler_b200.interface.functional.singular import fused_singular
 

@@ -201,6 +201,9 @@ def test_config3_fixed_modular(dev):
 
 
 def test_config4_graph_chain(dev):
+    """The benchmark's chain (workloads.config4_chain: drafting steps write their tokens in
+    place into the per-request table the verification reads) captured in one CUDA graph,
+    against the oracle replaying the same steps on the host."""
     from oracle import oracle
     from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
     from sonic_sampler_b200.interface.functional.multistep import prepare_multistep
@@ -212,47 +215,39 @@ def test_config4_graph_chain(dev):
     drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
     verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
     tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
-    # the verifier reads drafted tokens per request, the drafter per slot: use a slot-indexed
-    # token table for drafting and gather it for verification
-    slot_tokens = torch.zeros(b.top_k.numel(), gamma + 1, dtype=I32, device=dev)
-
-    def chain():
-        for t in range(gamma):
-            sel = drafter.drafting(w["draft_logits"][t], b, timestep=t, tokens=slot_tokens if t else None,
-                                   slot_mapping=sm, d2t_mapping=d2t, target_vocab=128256)
-            slot_tokens[sm.long(), t] = sel.tokens[:, 0]
-        tokens.copy_(slot_tokens[sm.long()])
-        return verifier(w["target_logits"], tokens, b, slot_mapping=sm, in_place=True)
 
     g = torch.cuda.CUDAGraph()
-    chain()  # warm-up outside capture
+    workloads.config4_chain(w, drafter, verifier, tokens)  # warm-up outside capture
     torch.cuda.synchronize()
-    slot_tokens.zero_()
     with torch.cuda.graph(g):
-        ver = chain()
-    slot_tokens.zero_()
+        ver = workloads.config4_chain(w, drafter, verifier, tokens)
+    tokens.fill_(-5)
     g.replay()
     torch.cuda.synchronize()
 
-    # oracle replay of the same chain on the host
+    # oracle replay of the same chain on the host (no repetition penalties: the drafting
+    # steps read no drafted tokens)
     hb = b.to("cpu")
-    hst = torch.zeros_like(slot_tokens, device="cpu")
+    htok = torch.full((active, gamma + 1), -5, dtype=I32)  # entries no step writes keep their value
     hsm, hd2t = sm.cpu(), d2t.cpu()
     for t in range(gamma):
         kw = buffer_kwargs(hb, timestep=t, draft=True)
         ref, args = prepare_singular(w["draft_logits"][t].cpu(), lookahead=gamma, target_vocab=128256,
-                                     block_n=drafter.tuning(active)[2], slot_mapping=hsm, d2t_mapping=hd2t,
-                                     drafted_tokens=hst if t else None, **kw)
+                                     block_n=drafter.tuning(active)[2], slot_mapping=hsm, d2t_mapping=hd2t, **kw)
         oracle.fused_singular(args)
-        hst[hsm.long(), t] = ref.tokens[:, 0]
-    htok = hst[hsm.long()].clone()
+        htok[:, t] = ref.tokens[:, 0]
+    drafted = htok[:, :gamma].clone()
     kw = buffer_kwargs(hb, timestep=None)
     rver, args = prepare_multistep(w["target_logits"].cpu(), kw.pop("indicators"), htok, lookahead=gamma,
                                    block_n=verifier.block_n, slot_mapping=hsm, output_tokens=htok, **kw)
     oracle.fused_multistep(args)
-    assert torch.equal(slot_tokens.cpu(), hst)
     assert torch.equal(ver.offsets.cpu(), rver.offsets)
     assert torch.equal(ver.tokens.cpu(), rver.tokens)
+    # the verified prefix of every request is its drafted tokens
+    got = tokens.cpu()
+    for i in range(active):
+        n = int(rver.offsets[i])
+        assert torch.equal(got[i, :n], drafted[i, :n])
 
 
 # ----------------------------------------------------------------------------------------
@@ -494,6 +489,88 @@ def test_plain_rows_no_processors(dev, vocab):
     x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=63)
     sel, ref, kw, kh = run_singular(x, **kw)
     assert_selection_equal(sel, ref, kw, kh)
+
+
+def _logits_only_multistep_kwargs(dev, batch, gamma, vocab, seed):
+    """Per-request parameters without grammar, counts or bias: every third request greedy
+    (with a temperature), the others stochastic with top-k / top-p / min-p and top-Z logprobs."""
+    from sonic_sampler_b200.core.flags import Indicator
+
+    params = workloads.config2_params(batch, seed)
+    ind = []
+    for i in range(batch):
+        f = Indicator.from_params(temperature=params.temperature[i], top_k=1 if i % 3 == 0 else params.top_k[i],
+                                  top_p=params.top_p[i], min_p=params.min_p[i], top_k_logprobs=4)
+        ind.append(int(f))
+    return dict(
+        indicators=torch.tensor(ind, dtype=torch.int32).to(torch.uint16).to(dev),
+        temperature=torch.tensor(params.temperature, dtype=BF16, device=dev),
+        top_k=torch.tensor(params.top_k, dtype=I32, device=dev),
+        top_p=torch.tensor(params.top_p, dtype=BF16, device=dev),
+        min_p=torch.tensor(params.min_p, dtype=BF16, device=dev),
+        top_k_logprobs=torch.full((batch,), 4, dtype=I32, device=dev),
+        gumbel_noise=workloads.log_exponential((batch, gamma + 1, vocab), dev, seed + 1),
+        uniform_noise=torch.rand(batch, gamma + 1, generator=torch.Generator().manual_seed(seed + 2))
+        .clamp_(min=torch.finfo(BF16).tiny).to(BF16).to(dev),
+    )
+
+
+@pytest.mark.parametrize("batch,varlen", [(128, False), (7, True)], ids=["multiwave", "varlen"])
+def test_multistep_logits_only(dev, batch, varlen):
+    """Multistep calls without grammar, counts or bias stream their rows through the
+    logits-only kernel (128 x 4 rows of 128256: a grid of several waves, one CTA per row;
+    varlen: one wave, several splits a row). Greedy and stochastic requests, drafts the target
+    partly accepts, a slot mapping; offsets, tokens and logprobs match the oracle bit for bit."""
+    gamma, vocab = 3, 128256
+    slots = batch + 5
+    kw = _logits_only_multistep_kwargs(dev, slots, gamma, vocab, seed=90 + batch)
+    sm = torch.randperm(slots, generator=torch.Generator().manual_seed(91))[:batch].to(I32).to(dev)
+    if varlen:
+        lengths = [1 + (i * 5) % (gamma + 1) for i in range(batch)]
+        cu = torch.tensor([0] + list(torch.tensor(lengths).cumsum(0)), dtype=I32)
+        rows = int(cu[-1])
+        x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=92)
+        tokens = x.float().argmax(-1).to(I32)
+        tokens[1::4] = (tokens[1::4] + 7) % vocab  # some drafts the target rejects
+        ver, ref, _, kh = run_multistep(x, tokens.contiguous(), cu_seqlens=cu.to(dev), lookahead=gamma,
+                                        slot_mapping=sm, block_n=4096, return_logprobs=True, max_top_logprobs=4,
+                                        **kw)
+        margins = cu[:-1].tolist()
+    else:
+        x = workloads.peaked_logits(batch * (gamma + 1), vocab, sigma=3.0, peaks=4, lift=12.0, device=dev,
+                                    seed=93).view(batch, gamma + 1, vocab)
+        tokens = x.float().argmax(-1).to(I32)
+        tokens[1::4, 1] = (tokens[1::4, 1] + 7) % vocab
+        ver, ref, _, kh = run_multistep(x, tokens.contiguous(), lookahead=gamma, slot_mapping=sm, block_n=4096,
+                                        return_logprobs=True, max_top_logprobs=4, **kw)
+        margins = [i * (gamma + 1) for i in range(batch)]
+    _verify_logprobs_equal(ver, ref, kh["indicators"], sm.cpu().tolist(), margins)
+    assert int(ver.offsets.max()) >= 1
+
+
+def test_multistep_logits_only_greedy_floor_edges(dev):
+    """Greedy multistep rows on the logits-only kernel's floor test: ties made by the
+    temperature, NaN logits, an all -inf row, two +inf values, a +-0 maximum, and a request
+    without temperature."""
+    gamma, vocab, batch = 1, 128256, 4
+    rows = batch * (gamma + 1)
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=95)
+    g = torch.Generator().manual_seed(95)
+    near = torch.randperm(vocab, generator=g)[:64]
+    x[0, near] = (torch.full((64,), 20.0) + torch.arange(64) * 0.0625).to(BF16).to(dev)
+    x[1, torch.randperm(vocab, generator=g)[:5]] = float("nan")
+    x[2] = float("-inf")
+    x[3, 777] = float("inf")
+    x[3, 90001] = float("inf")
+    x[4] = -x[4].abs() - 1.0
+    x[4, 5000] = -0.0
+    x[4, 70000] = 0.0
+    ind = torch.tensor([0x60, 0x60, 0x60, 0x40], dtype=torch.int32).to(torch.uint16).to(dev)
+    kw = dict(indicators=ind, temperature=torch.tensor([3.0, 0.9, 0.6, 1.0], dtype=BF16, device=dev),
+              gumbel_noise=torch.zeros(batch, gamma + 1, vocab, dtype=BF16, device=dev),
+              uniform_noise=torch.ones(batch, gamma + 1, dtype=BF16, device=dev))
+    tokens = x.float().nan_to_num(nan=-1e30).argmax(-1).to(I32)
+    run_multistep(x, tokens.contiguous(), lookahead=gamma, block_n=1024, **kw)
 
 
 # ----------------------------------------------------------------------------------------

@@ -117,6 +117,42 @@ def test_multistep_wait_timeout_writes_nothing_and_is_reported(dev):
     assert ops.workspace_error(ws) == 0
 
 
+def test_multistep_logits_only_wait_timeout(dev):
+    """The same for multistep rows on the logits-only kernel (no grammar, counts or bias)."""
+    from oracle import oracle
+    from sonic_sampler_b200 import _abi, ops
+    from sonic_sampler_b200.interface.functional.multistep import fused_multistep, prepare_multistep
+
+    batch, gamma, vocab = 8, 3, 128256
+    x = workloads.peaked_logits(batch * (gamma + 1), vocab, sigma=3.0, peaks=4, lift=12.0, device=dev,
+                                seed=24).view(batch, gamma + 1, vocab)
+    tokens = x.float().argmax(-1).to(torch.int32).contiguous()
+    ind = torch.tensor([0x60, 0x1A0] * (batch // 2), dtype=torch.int32).to(torch.uint16).to(dev)
+    kw = dict(temperature=torch.full((batch,), 0.8, dtype=torch.bfloat16, device=dev),
+              top_k=torch.full((batch,), 40, dtype=torch.int32, device=dev),
+              top_p=torch.full((batch,), 0.9, dtype=torch.bfloat16, device=dev),
+              gumbel_noise=workloads.log_exponential((batch, gamma + 1, vocab), dev, 25),
+              uniform_noise=torch.full((batch, gamma + 1), 0.5, dtype=torch.bfloat16, device=dev),
+              lookahead=gamma, block_n=4096)
+    ws = ops.new_workspace(ops.multistep_workspace_bytes(batch, gamma, vocab), dev)
+    ver, args = prepare_multistep(x, ind, tokens.clone(), scratchpad=ws, **kw)
+    ver.offsets.fill_(SENTINEL)
+    args.flags |= _abi.FLAG_DEBUG_STALL_RING
+    _launch("sonic_fused_multistep", args)
+    torch.cuda.synchronize()
+    assert bool((ver.offsets == SENTINEL).all())
+    assert ops.workspace_error(ws) & _abi.DEVICE_ERR_WAIT
+
+    good = fused_multistep(x, ind, tokens.clone(), scratchpad=ws, **kw)
+    hk = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in kw.items()}
+    ref, rargs = prepare_multistep(x.cpu(), ind.cpu(), tokens.cpu().clone(), **hk)
+    oracle.fused_multistep(rargs)
+    torch.cuda.synchronize()
+    assert torch.equal(good.offsets.cpu(), ref.offsets)
+    assert torch.equal(good.tokens.cpu(), ref.tokens)
+    assert ops.workspace_error(ws) == 0
+
+
 def test_static_entry_reports_into_the_library_word(dev):
     from sonic_sampler_b200 import _abi, ops
     from sonic_sampler_b200.interface.functional.singular import prepare_singular
