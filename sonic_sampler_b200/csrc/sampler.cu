@@ -1736,6 +1736,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 
   uint64_t* lists = ws.cand + (uint64_t)r * splits * kMaxK;
   if (greedy) {
+    pc.flush(warp, lane);
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
     if (__syncthreads_or(werr)) {
@@ -2187,6 +2188,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   // one CTA covers the whole row: no workspace list, no ticket, no merge across CTAs
   const bool whole_row = !MS && splits == 1;
   if (greedy) {
+    pc.flush(warp, lane);
     best = warp_max_u64(best);
     if (lane == 0) atomicMax(&st.best, (unsigned long long)best);
     if (__syncthreads_or(werr)) {

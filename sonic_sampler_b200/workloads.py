@@ -225,7 +225,8 @@ def runner(name: str, device):
     interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep; 4: three
     cross-vocabulary greedy drafting steps and a greedy verification, as one chain;
     5: fused_singular with Philox noise; 1: UnshardedBoundedTopK; indexed_copy: the noise
-    staging of GumbelNoise.stage_weights)."""
+    staging of GumbelNoise.stage_weights; config4_verify[_logits_only]: config 4's verification
+    step alone)."""
     dev = torch.device(device)
     if name == "config1":
         from sonic_sampler_b200.interface import UnshardedBoundedTopK
@@ -261,6 +262,26 @@ def runner(name: str, device):
         verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
         tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
         return lambda: config4_chain(c, drafter, verifier, tokens)
+    if name in ("config4_verify", "config4_verify_logits_only"):
+        # the chain's verification step alone, on drafted tokens the target partly accepts:
+        # through UnshardedFusedMultistep with the buffers (the rows kernel sees grammar, count
+        # and bias buffers, so its rows take singular_kernel), or through fused_multistep with
+        # the per-slot scalars only (the rows take the logits-only kernel)
+        from sonic_sampler_b200.interface import UnshardedFusedMultistep
+        from sonic_sampler_b200.interface.functional.multistep import fused_multistep
+
+        c = config4(dev, seed=10)
+        b, gamma, sm = c["buffers"], c["gamma"], c["slot_mapping"]
+        active = sm.numel()
+        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        tokens = c["target_logits"].float().argmax(-1).to(I32)
+        tokens[1::3, 1] = (tokens[1::3, 1] + 1) % 128256
+        if name == "config4_verify":
+            return lambda: verifier(c["target_logits"], tokens, b, slot_mapping=sm)
+        return lambda: fused_multistep(c["target_logits"], b.flags.target, tokens, slot_mapping=sm, lookahead=gamma,
+                                       temperature=b.temperature, top_k=b.top_k, top_p=b.top_p, min_p=b.min_p,
+                                       gumbel_noise=b.weights.gumbel.target, uniform_noise=b.weights.uniform,
+                                       block_n=verifier.block_n, scratchpad=verifier.scratchpad)
     if name == "config5":
         from sonic_sampler_b200.interface.functional.singular import fused_singular
 
