@@ -220,25 +220,26 @@ def config5(device, seed: int = 0, batch: int = 1024, vocab: int = 256000):
     )
 
 
-def runner(name: str, device):
+def runner(name: str, device, pdl: bool = True):
     """A no-argument callable that runs benchmark config `name` once through the public
     interface (config 2: UnshardedFusedSingular.autoregressive; 3: fused_multistep; 4: three
     cross-vocabulary greedy drafting steps and a greedy verification, as one chain;
     5: fused_singular with Philox noise; 1: UnshardedBoundedTopK; indexed_copy: the noise
     staging of GumbelNoise.stage_weights; config4_verify[_logits_only]: config 4's verification
-    step alone)."""
+    step alone). `pdl` sets the programmatic-dependent-launch attribute of the sampler launches
+    (the interface objects' `pdl`, the functional calls' `enable_pdl`)."""
     dev = torch.device(device)
     if name == "config1":
         from sonic_sampler_b200.interface import UnshardedBoundedTopK
 
         c = config1(dev)
-        topk = UnshardedBoundedTopK.initialize(32000, batch_size=8, k=c["k"])
+        topk = UnshardedBoundedTopK.initialize(32000, batch_size=8, k=c["k"], pdl=pdl)
         return lambda: topk(c["logits"])
     if name == "config2":
         from sonic_sampler_b200.interface import UnshardedFusedSingular
 
         c = config2(dev, seed=1000)
-        sampler = UnshardedFusedSingular.initialize(128256, batch_size=64)
+        sampler = UnshardedFusedSingular.initialize(128256, batch_size=64, pdl=pdl)
         return lambda: sampler.autoregressive(c["logits"], c["buffers"], logprobs=True)
     if name == "config3":
         from sonic_sampler_b200.interface.functional.multistep import fused_multistep
@@ -252,14 +253,14 @@ def runner(name: str, device):
                   top_k_logprobs=b.top_logprobs, gumbel_noise=b.weights.gumbel.target, uniform_noise=b.weights.uniform)
         return lambda: fused_multistep(c["flat_logits"], b.flags.target, c["flat_tokens"], cu_seqlens=c["cu_seqlens"],
                                        lookahead=c["gamma"], max_top_logprobs=20, return_logprobs=True,
-                                       draft_probabilities=c["probabilities"], block_n=4096, **kw)
+                                       draft_probabilities=c["probabilities"], block_n=4096, enable_pdl=pdl, **kw)
     if name == "config4":
         from sonic_sampler_b200.interface import UnshardedFusedMultistep, UnshardedFusedSingular
 
         c = config4(dev, seed=10)
         active, gamma = c["slot_mapping"].numel(), c["gamma"]
-        drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma)
-        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        drafter = UnshardedFusedSingular.initialize(32000, batch_size=active, lookahead=gamma, pdl=pdl)
+        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active, pdl=pdl)
         tokens = torch.zeros(active, gamma + 1, dtype=I32, device=dev)
         return lambda: config4_chain(c, drafter, verifier, tokens)
     if name in ("config4_verify", "config4_verify_logits_only"):
@@ -273,7 +274,7 @@ def runner(name: str, device):
         c = config4(dev, seed=10)
         b, gamma, sm = c["buffers"], c["gamma"], c["slot_mapping"]
         active = sm.numel()
-        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active)
+        verifier = UnshardedFusedMultistep.initialize(128256, lookahead=gamma, batch_size=active, pdl=pdl)
         tokens = c["target_logits"].float().argmax(-1).to(I32)
         tokens[1::3, 1] = (tokens[1::3, 1] + 1) % 128256
         if name == "config4_verify":
@@ -281,13 +282,13 @@ def runner(name: str, device):
         return lambda: fused_multistep(c["target_logits"], b.flags.target, tokens, slot_mapping=sm, lookahead=gamma,
                                        temperature=b.temperature, top_k=b.top_k, top_p=b.top_p, min_p=b.min_p,
                                        gumbel_noise=b.weights.gumbel.target, uniform_noise=b.weights.uniform,
-                                       block_n=verifier.block_n, scratchpad=verifier.scratchpad)
+                                       block_n=verifier.block_n, scratchpad=verifier.scratchpad, enable_pdl=pdl)
     if name == "config5":
         from sonic_sampler_b200.interface.functional.singular import fused_singular
 
         c = config5(dev, seed=1)
         kw = dict(indicators=c["indicators"], top_k=c["top_k"], top_p=c["top_p"], block_n=4096,
-                  philox_seed=c["philox_seed"], philox_offset=17, return_logprobs=True)
+                  philox_seed=c["philox_seed"], philox_offset=17, return_logprobs=True, enable_pdl=pdl)
         return lambda: fused_singular(c["logits"], **kw)
     if name == "indexed_copy":
         from sonic_sampler_b200.core.buffers import GumbelNoise
@@ -303,13 +304,45 @@ def runner(name: str, device):
     raise ValueError(f"unknown workload {name!r}")
 
 
-if __name__ == "__main__":
-    # python -m sonic_sampler_b200.workloads config5 [calls]: run a config `calls` times on
-    # cuda:0 (the target of the ncu commands that produced the profiles)
-    import sys
-
-    fn = runner(sys.argv[1], "cuda")
-    for _ in range(int(sys.argv[2]) if len(sys.argv) > 2 else 6):
+def time_calls(fn, calls: int = 30, flush_bytes: int = 256 << 20) -> list[float]:
+    """Microseconds of `calls` CUDA-graph replays of one captured `fn()`, each after an L2
+    flush (a write of `flush_bytes`), timed with CUDA events on the replaying stream."""
+    for _ in range(3):
         fn()
     torch.cuda.synchronize()
-    print("ok", sys.argv[1])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    flush = torch.empty(flush_bytes, dtype=torch.uint8, device="cuda")
+    out = []
+    for i in range(calls):
+        flush.fill_(i & 0xFF)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        graph.replay()
+        end.record()
+        torch.cuda.synchronize()
+        out.append(start.elapsed_time(end) * 1e3)
+    return out
+
+
+if __name__ == "__main__":
+    # python -m sonic_sampler_b200.workloads <config> [calls]: run a config `calls` times on
+    # cuda:0 (the target of the ncu commands that produced the profiles).
+    # python -m sonic_sampler_b200.workloads <config> --time [--pdl off]: median and minimum
+    # of 30 CUDA-graph replays, L2 flushed before each.
+    import statistics
+    import sys
+
+    args = sys.argv[1:]
+    pdl_on = not ("--pdl" in args and args[args.index("--pdl") + 1] == "off")
+    fn = runner(args[0], "cuda", pdl=pdl_on)
+    if "--time" in args:
+        ts = time_calls(fn)
+        print(f"{args[0]} pdl={'on' if pdl_on else 'off'}: median {statistics.median(ts):.1f} us, "
+              f"min {min(ts):.1f} us over {len(ts)} graph replays")
+    else:
+        for _ in range(int(args[1]) if len(args) > 1 else 6):
+            fn()
+        torch.cuda.synchronize()
+        print("ok", args[0])
