@@ -40,7 +40,8 @@ constexpr int VPT = 8;                     // consecutive columns per thread per
 constexpr int CH = NT * VPT;               // columns per chunk (single-row kernels)
 constexpr int STAGES = 4;                  // bulk-copy ring depth (stages of every stream)
 constexpr int TARGET_CTAS = 296;           // 148 SMs x 2 resident CTAs: one wave
-constexpr int MAX_SPLIT_COLS = 65536;      // local column index fits 16 bits
+constexpr int MAX_SPLIT_COLS = 65536;      // columns of a split in one-wave grids
+constexpr int SPLIT_MAX_COLS = 256 * CH;   // columns one CTA of the general kernel can cover
 constexpr int MAX_SPLITS = 32;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls of a bulk-copy barrier before giving up
 constexpr int MS_MAX_STEPS = SONIC_MAX_LOOKAHEAD + 1;
@@ -1211,7 +1212,10 @@ __device__ __forceinline__ void select_row(const SonicSingularArgs& a, int64_t r
 // (ops/prologue.py:272 + ops/singular.py:154)
 // ---------------------------------------------------------------------------------------
 
-template <int MODE, bool INDIRECT, bool MS>
+// WIDE: a CTA covers more than 65536 columns (grids of several waves, one CTA per row): its
+// warps' keys carry warp-local column indices and are folded as 64-bit global keys. Otherwise
+// (cols <= 65536) the keys carry the CTA-local column and the fold runs on 32-bit keys.
+template <int MODE, bool INDIRECT, bool MS, bool WIDE = false>
 __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a, int splits, int cols, int log2bn,
                                                       Workspace ws, uint64_t* cand_out, const MsRows ms) {
   __shared__ __align__(16) RowSmem<uint32_t, SQCAP> st;
@@ -1222,6 +1226,14 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   const SonicSamplingParams& P = a.params;
   const int64_t c0 = (int64_t)split * cols;
   const int64_t c1 = min((int64_t)a.vocab_size, c0 + cols);
+  // The 16-bit column index of a key. WIDE: warp-local, column c0 + 2048 k + 256 w + i (warp
+  // w's group in chunk k, i < 256) is (k << 8) | i, so a CTA covers up to 256 chunks
+  // (SPLIT_MAX_COLS columns), and keys of different warps meet only as 64-bit keys with global
+  // columns (the end-of-split fold). Else the CTA-local column c - c0 (< 65536).
+  auto wloc = [&](int64_t c) {
+    const uint32_t d = (uint32_t)(c - c0);
+    return WIDE ? (((d >> 11) << 8) | (d & (GROUP - 1))) : d;
+  };
   PhaseClock pc;
   pc.stamp(PS_ENTRY, tid == 0);
 
@@ -1449,7 +1461,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
       const uint32_t h = half_of(raw.x, j);
-      key[j] = (enc16(h) << 16) | (uint32_t)(0xffff - (int)(c + j - c0));
+      key[j] = (enc16(h) << 16) | (0xffffu - wloc(c + j));
       if (j < nvalid && bf2f((uint16_t)h) >= thr) m |= 1u << j;
     }
     int pos = reserve(__popc(m));
@@ -1520,7 +1532,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
         }
       }
       int pos = reserve(__popc(m));
-      const uint32_t base = (uint32_t)(0xffff - (int)(c - c0));
+      const uint32_t base = 0xffffu - wloc(c);
       pc.count(PW_PUSHED, (unsigned long long)__popc(m));
       while (m) {
         const int j = __ffs(m) - 1;
@@ -1591,7 +1603,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       const int64_t dl = (int64_t)st.toks[t] - (gcol(warp) + shard);
       if (dl >= 0 && dl < VPT) ok &= ~(1u << dl);
     }
-    const uint32_t base = (uint32_t)(0xffff - (int)(gcol(warp) - c0));
+    const uint32_t base = 0xffffu - wloc(gcol(warp));
     uint32_t lm = 0;
 #pragma unroll
     for (int j = 0; j < VPT; ++j) {
@@ -1756,14 +1768,39 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       fail_split();
       return;
     }
-    uint32_t fin[4];
-    block_fold(st.lists, warp, lane, fin);
+    // the split's top-128 as 64-bit keys with global columns (in warp 0). WIDE: every warp's
+    // list is converted first, laid out [NW][128] over the queues (free now), then folded
+    // across the warps; else the 32-bit lists are folded and converted
+    auto fold_warps = [&](uint64_t (&out)[4]) {
+      if constexpr (WIDE) {
+        uint64_t (*lists64)[kMaxK] = reinterpret_cast<uint64_t (*)[kMaxK]>(&st.queue[0][0]);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint32_t key = st.lists[warp][4 * lane + i];
+          uint64_t gk = 0;
+          if (key) {
+            const uint32_t loc = 0xffffu - (key & 0xffffu);
+            const int64_t col = c0 + ((int64_t)(loc >> 8) << 11) + (int64_t)warp * GROUP + (loc & (GROUP - 1));
+            gk = ((uint64_t)(key >> 16) << 32) | (uint64_t)(0xffffffffu - (uint32_t)col);
+          }
+          lists64[warp][4 * lane + i] = gk;
+        }
+        block_fold<uint64_t>(lists64, warp, lane, out);
+      } else {
+        uint32_t f[4];
+        block_fold(st.lists, warp, lane, f);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) out[j] = to_global<uint32_t>(f[j], c0);
+      }
+    };
+    uint64_t fin[4];
+    fold_warps(fin);
     pc.stamp(PS_FOLD, tid == 0);
     if (warp == 0) {
       // the split holds at least kk finite candidates when list position kk - 1 is taken
       const int jj = (kk - 1) & 3;
-      const uint32_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
-      const uint32_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
+      const uint64_t f = jj == 0 ? fin[0] : (jj == 1 ? fin[1] : (jj == 2 ? fin[2] : fin[3]));
+      const uint64_t last = __shfl_sync(kFull, f, (kk - 1) >> 2);
       if (lane == 0) st.flag = last != 0;
     }
     __syncthreads();
@@ -1783,13 +1820,14 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       }
       if (w.qn) wtk_absorb(w, q, lane);
       if (lane == 0) st.qn[warp] = 0;
-      block_fold(st.lists, warp, lane, fin);
+      __syncthreads();
+      fold_warps(fin);
     }
     if (warp == 0) {
       uint64_t* out = lists + (int64_t)split * kMaxK;
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint64_t key = to_global<uint32_t>(fin[j], c0);
+        const uint64_t key = fin[j];
         stcg64(out + 4 * lane + j, key);
         // warm L2 with the noise the merge will gather for this candidate (multistep rows
         // draw their noise in ms_verify_kernel: their launch carries no noise pointer)
@@ -2875,6 +2913,22 @@ static sonic_status check_singular(const SonicSingularArgs* a, bool selects) {
   return SONIC_OK;
 }
 
+// The general kernel's splits: grids of several waves pay every CTA's fixed costs (row set-up,
+// first-chunk latency, the split's end) once per CTA, so they take as few splits as keep the
+// TARGET_CTAS slots busy, down to one CTA per row (at most SPLIT_MAX_COLS columns a CTA). Never
+// more splits than the workspace was sized for (p.splits).
+static Plan wave_plan(const Plan& p, int64_t rows, int64_t V) {
+  if ((int64_t)p.splits * rows <= TARGET_CTAS) return p;
+  int64_t sp = std::max<int64_t>(1, std::min<int64_t>(p.splits, TARGET_CTAS / std::max<int64_t>(1, rows)));
+  sp = std::max<int64_t>(sp, (V + SPLIT_MAX_COLS - 1) / SPLIT_MAX_COLS);
+  int64_t wc = (V + sp - 1) / sp;
+  wc = (wc + CH - 1) / CH * CH;
+  Plan w;
+  w.splits = (int)((V + wc - 1) / wc);
+  w.cols = (int)wc;
+  return w;
+}
+
 // Rows with no per-column processor anywhere in the call stream through the logits-only
 // kernel: the rows of a singular call, their vocab-sharded candidates (`cand`), or the rows of a
 // multistep call (`ms`). `used` gets the column splits of the launch (at most p.splits, so
@@ -2937,21 +2991,28 @@ static sonic_status singular_launch(const SonicSingularArgs* a, void* stream, ui
   int mode = (xvec && (ind || params_vec_ok(a->params, a->shard_offset))) ? kVec : kScalar;
   // with a d2t table the ring streams the logits only, which xvec already allows
   if (mode == kVec && (ind || params_tma_ok(a->params, a->shard_offset))) mode = kTma;
-  dim3 grid(p.splits, a->rows);
+  // ring grids of several waves: one CTA per row where the row fits (wide keys)
+  const Plan wp = mode == kTma ? wave_plan(p, a->rows, a->vocab_size) : p;
+  const bool wide = wp.cols > MAX_SPLIT_COLS;
+  dim3 grid(wp.splits, a->rows);
   cudaStream_t st = (cudaStream_t)stream;
   const bool pdl = (a->flags & SONIC_FLAG_PDL) != 0;
   const int l2 = ilog2(a->block_n);
   const size_t ring = mode == kTma ? (size_t)RING_BYTES : 0;
+  const int sp = wp.splits, sc = wp.cols;
   cudaError_t e;
   if (ind)
-    e = mode == kTma  ? launch(singular_kernel<kTma, true, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
-        : mode == kVec ? launch(singular_kernel<kVec, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
-                       : launch(singular_kernel<kScalar, true, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
+    e = mode == kTma
+            ? (wide ? launch(singular_kernel<kTma, true, false, true>, grid, ring, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{})
+                    : launch(singular_kernel<kTma, true, false>, grid, ring, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{}))
+        : mode == kVec ? launch(singular_kernel<kVec, true, false>, grid, 0, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{})
+                       : launch(singular_kernel<kScalar, true, false>, grid, 0, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{});
   else if (mode == kTma)
-    e = launch(singular_kernel<kTma, false, false>, grid, ring, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
+    e = wide ? launch(singular_kernel<kTma, false, false, true>, grid, ring, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{})
+             : launch(singular_kernel<kTma, false, false>, grid, ring, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{});
   else
-    e = mode == kVec ? launch(singular_kernel<kVec, false, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{})
-                     : launch(singular_kernel<kScalar, false, false>, grid, 0, st, pdl, *a, p.splits, p.cols, l2, ws, cand, MsRows{});
+    e = mode == kVec ? launch(singular_kernel<kVec, false, false>, grid, 0, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{})
+                     : launch(singular_kernel<kScalar, false, false>, grid, 0, st, pdl, *a, sp, sc, l2, ws, cand, MsRows{});
   return check_launch(e, what);
 }
 
@@ -3082,18 +3143,22 @@ sonic_status sonic_fused_multistep(const SonicMultistepArgs* a, void* stream) {
   const bool xvec = aligned(a->logits, 16) && (a->logits_stride % 8) == 0;
   int mode = (xvec && params_vec_ok(a->params, a->shard_offset)) ? kVec : kScalar;
   if (mode == kVec && params_tma_ok(a->params, a->shard_offset)) mode = kTma;
-  const dim3 grid(p.splits, (unsigned)rows);
+  const Plan wp = mode == kTma ? wave_plan(p, rows, a->vocab_size) : p;
+  const bool wide = wp.cols > MAX_SPLIT_COLS;
+  const dim3 grid(wp.splits, (unsigned)rows);
   cudaError_t e;
   if (mode == kTma)
-    e = launch(singular_kernel<kTma, false, true>, grid, (size_t)RING_BYTES, st, pdl, sa, p.splits, p.cols, l2, ws,
-               (uint64_t*)nullptr, m);
+    e = wide ? launch(singular_kernel<kTma, false, true, true>, grid, (size_t)RING_BYTES, st, pdl, sa, wp.splits, wp.cols,
+                      l2, ws, (uint64_t*)nullptr, m)
+             : launch(singular_kernel<kTma, false, true>, grid, (size_t)RING_BYTES, st, pdl, sa, wp.splits, wp.cols, l2,
+                      ws, (uint64_t*)nullptr, m);
   else if (mode == kVec)
-    e = launch(singular_kernel<kVec, false, true>, grid, 0, st, pdl, sa, p.splits, p.cols, l2, ws, (uint64_t*)nullptr, m);
+    e = launch(singular_kernel<kVec, false, true>, grid, 0, st, pdl, sa, wp.splits, wp.cols, l2, ws, (uint64_t*)nullptr, m);
   else
-    e = launch(singular_kernel<kScalar, false, true>, grid, 0, st, pdl, sa, p.splits, p.cols, l2, ws,
+    e = launch(singular_kernel<kScalar, false, true>, grid, 0, st, pdl, sa, wp.splits, wp.cols, l2, ws,
                (uint64_t*)nullptr, m);
   if (sonic_status s = check_launch(e, "sonic_fused_multistep (rows)")) return s;
-  e = launch(ms_verify_kernel, dim3(a->batch_size), 0, st, pdl, *a, p.splits, l2, ws);
+  e = launch(ms_verify_kernel, dim3(a->batch_size), 0, st, pdl, *a, wp.splits, l2, ws);
   return check_launch(e, "sonic_fused_multistep");
 }
 

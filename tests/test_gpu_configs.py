@@ -778,3 +778,56 @@ def test_multiwave_logits_only_sub_splits(dev):
     assert torch.equal(torch.isnan(a), torch.isnan(b))
     assert torch.equal(bits(a)[~torch.isnan(a)], bits(b)[~torch.isnan(b)])
     assert torch.equal(sel.logprobs.top_k.tokens[sample].cpu()[stoch], ref.logprobs.top_k.tokens[stoch])
+
+
+def test_multiwave_general_kernel_one_cta_per_row(dev):
+    """Calls with every processor whose grid would take several waves stream each row in one
+    CTA of the general kernel (320 rows of V = 200003: one CTA covers all 98 chunks, its
+    warps' keys carry warp-local column indices and meet only as 64-bit keys with global
+    columns). Mixed greedy and stochastic rows with top-k / top-p / min-p, counts, bias,
+    grammar and logprobs; a sample of rows matches the oracle bit for bit."""
+    from oracle import oracle
+    from sonic_sampler_b200.interface.functional.singular import fused_singular, prepare_singular
+
+    rows, vocab = 320, 200003
+    b = _params(dev, rows, vocab, seed=81, top_logprobs=4)
+    ind = b.flags.target.cpu().to(torch.int32)
+    ind[::7] = (ind[::7] & 0x3F) | 0x40  # some greedy rows
+    b.flags.packed[:, 0] = ind.to(torch.uint16).to(dev)
+    x = workloads.peaked_logits(rows, vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=82)
+    kw = buffer_kwargs(b)
+    kw.update(return_logprobs=True, max_top_logprobs=4, logprobs_dtype=F32, block_n=4096)
+    sel = fused_singular(x, **kw)
+    torch.cuda.synchronize()
+    sample = torch.arange(0, rows, 11)
+    kh = host(kw)
+    kh["slot_mapping"] = sample.to(I32)
+    ref, args = prepare_singular(x[sample.to(dev)].cpu(), **kh)
+    oracle.fused_singular(args)
+    assert torch.equal(sel.tokens[sample].cpu(), ref.tokens)
+    stoch = ~(ind[sample] & 0x40).bool()
+    a, r = sel.logprobs.selected[sample].cpu()[stoch], ref.logprobs.selected[stoch]
+    assert torch.equal(torch.isnan(a), torch.isnan(r))
+    assert torch.equal(bits(a)[~torch.isnan(a)], bits(r)[~torch.isnan(r)])
+    assert torch.equal(sel.logprobs.top_k.tokens[sample].cpu()[stoch], ref.logprobs.top_k.tokens[stoch])
+
+
+def test_multiwave_multistep_rows_one_cta_per_row(dev):
+    """A multistep call with every processor and 128 requests x 5 rows (a grid of several
+    waves: one CTA per row of the general kernel in multistep mode), stochastic and greedy
+    requests with draft probabilities: offsets, tokens, counts and logprobs match the oracle."""
+    gamma, vocab, batch = 4, 128256, 128
+    b = workloads.sampling_buffers(batch, gamma + 1, vocab, dev, 83, workloads.config2_params(batch, 84),
+                                   top_logprobs=3)
+    ind = b.flags.target.cpu().to(torch.int32)
+    ind[::5] = (ind[::5] & 0x3F) | 0x40
+    b.flags.packed[:, 0] = ind.to(torch.uint16).to(dev)
+    x = workloads.peaked_logits(batch * (gamma + 1), vocab, sigma=3.0, peaks=4, lift=12.0, device=dev,
+                                seed=85).view(batch, gamma + 1, vocab)
+    tokens = x.float().argmax(-1).to(I32)
+    tokens[1::3, 2] = (tokens[1::3, 2] + 3) % vocab
+    q = torch.softmax(x[:, :gamma].float(), -1).contiguous()
+    kw = buffer_kwargs(b, timestep=None)
+    ver, ref, kw, kh = run_multistep(x, tokens.contiguous(), lookahead=gamma, block_n=4096, update_counts=True,
+                                     return_logprobs=True, max_top_logprobs=3, draft_probabilities=q, **kw)
+    _verify_logprobs_equal(ver, ref, kh["indicators"], list(range(batch)), [i * (gamma + 1) for i in range(batch)])
