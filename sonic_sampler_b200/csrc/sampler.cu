@@ -42,6 +42,9 @@ constexpr int STAGES = 4;                  // bulk-copy ring depth (stages of ev
 constexpr int TARGET_CTAS = 296;           // 148 SMs x 2 resident CTAs: one wave
 constexpr int MAX_SPLIT_COLS = 65536;      // columns of a split in one-wave grids
 constexpr int SPLIT_MAX_COLS = 256 * CH;   // columns one CTA of the general kernel can cover
+constexpr int WIDE_GROUPS = 2;             // groups a warp takes from one wide chunk (greedy rows)
+constexpr int WIDE_GROUPS_LONG = 4;        // the same for CTAs of at least WIDE_LONG_COLS columns
+constexpr int WIDE_LONG_COLS = 32 * CH;
 constexpr int MAX_SPLITS = 32;
 constexpr uint32_t WAIT_LIMIT = 1u << 22;  // polls of a bulk-copy barrier before giving up
 constexpr int MS_MAX_STEPS = SONIC_MAX_LOOKAHEAD + 1;
@@ -1313,10 +1316,14 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   // (8 KB) of logits: a warp then handles two adjacent groups per chunk, so the stage wait and
   // release are paid once per 512 columns of this almost free per-column work. Such a row
   // needs one full wide chunk (chunk 0's first half is already on its way).
+  // Long CTAs take wider chunks still (WIDE_GROUPS_LONG groups a warp); short ones keep two,
+  // which leaves fewer columns to the direct-load tail after the last full chunk.
+  const int wg = (c1 - c0) >= WIDE_LONG_COLS ? WIDE_GROUPS_LONG : WIDE_GROUPS;
   const bool wide = MODE == kTma && (ind & 0x40) && !cand_out && !rc.nd.proc && sg_stage == CH * 2 &&
-                    (!rc.nd.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f)) && (c1 - c0) >= 2 * CH;
-  const int cw = wide ? 2 * CH : CH;                   // columns of a ring chunk
-  const int stage_bytes = wide ? 4 * CH : sg_stage;  // bytes of a ring stage
+                    (!rc.nd.temp || (rc.temp > 0.0f && rc.temp <= 3.3895313892515355e+38f)) &&
+                    (c1 - c0) >= wg * CH;
+  const int cw = wide ? wg * CH : CH;                   // columns of a ring chunk
+  const int stage_bytes = wide ? wg * CH * 2 : sg_stage;  // bytes of a ring stage
   const int nst = min(MAX_RING_STAGES, RING_BYTES / stage_bytes);
   const int nck = MODE == kTma ? (int)((c1 - c0) / cw) : 0;  // ring chunks of this split
   auto issue_chunk = [&](int i, int stage) {  // one thread
@@ -1327,8 +1334,8 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     if (i == 0) {
       // the first 2048 columns' logits are on their way already
       if (wide) {
-        mbar_expect_tx(bar, (uint32_t)(CH * 2));
-        bulk_load(sp + CH * 2, xrow + cc + CH, CH * 2, bar);
+        mbar_expect_tx(bar, (uint32_t)((wg - 1) * CH * 2));
+        bulk_load(sp + CH * 2, xrow + cc + CH, (uint32_t)((wg - 1) * CH * 2), bar);
       } else if (sg_stage > CH * 2) {
         mbar_expect_tx(bar, (uint32_t)(sg_stage - CH * 2));
       } else {
@@ -1617,16 +1624,16 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   }
   int stage = 0;
   uint32_t phase = 0;
-  // wide chunks (greedy rows): groups 2 * NW * k + 2 * warp and the next one
+  // wide chunks (greedy rows): groups wg * (NW * k + warp) and the next wg - 1
   for (int k = 0; k < (wide && !werr ? nck : 0); ++k) {
     if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
       give_up();
       break;
     }
-    const unsigned char* sp = smem_ring + stage * stage_bytes + warp * (GROUP * 4) + lane * 16;
-    const int g0 = 2 * NW * k + 2 * warp;
+    const unsigned char* sp = smem_ring + stage * stage_bytes + warp * (GROUP * 2 * wg) + lane * 16;
+    const int g0 = wg * (NW * k + warp);
 #pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < wg; ++h) {
       Raw8 raw;
       const uint4 xq = *reinterpret_cast<const uint4*>(sp + h * (GROUP * 2));
       raw.x[0] = xq.x; raw.x[1] = xq.y; raw.x[2] = xq.z; raw.x[3] = xq.w;
@@ -1650,7 +1657,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
     }
   }
   // the remaining groups: standard ring chunks, then direct loads
-  for (int k = 0, g = (wide ? 2 * NW * nck : 0) + warp; g < ngroups && !werr; ++k, g += NW) {
+  for (int k = 0, g = (wide ? wg * NW * nck : 0) + warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
     const int nv = gvalid(g);
     Raw8 raw;
