@@ -2565,6 +2565,8 @@ struct MsSmem {
   float qd[MS_MAX_STEPS];  // draft probability of each drafted token (stochastic drafts)
   float prob[MS_MAX_STEPS][kMaxK];
   int32_t cand[MS_MAX_STEPS][kMaxK];
+  float qc[MS_MAX_STEPS][kMaxK];     // draft probability of each candidate (stochastic drafts)
+  uint16_t gc[MS_MAX_STEPS][kMaxK];  // rejection noise of each candidate (buffered noise)
   int64_t gsel[MS_MAX_STEPS];
 };
 
@@ -2618,13 +2620,10 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
   __syncthreads();
 
   pdl_wait();
-  // a CTA of this request's rows gave up a bounded wait (singular_kernel's error path): the
-  // request writes no outputs; its mark is cleared for the next call
-  if (ldcg32(ws.tickets + b) != 0) {
-    __syncthreads();
-    if (tid == 0) ws.tickets[b] = 0;
-    return;
-  }
+  // A CTA of this request's rows gave up a bounded wait (singular_kernel's error path): the
+  // request writes no outputs, and its mark is cleared for the next call. The mark is loaded
+  // together with the rows' lists and checked before the first output is written.
+  const uint32_t failed = ldcg32(ws.tickets + b);
 
   // ---- per-row merge (warp w handles rows w, w+8, ...) ----
   for (int s = warp; s < T; s += NT / 32) {
@@ -2636,7 +2635,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       const int64_t g = greedy_col(bk, log2bn);
       if (lane == 0) {
         sm.gsel[s] = g;
-        if (a.indices) a.indices[margin * kMaxK + s] = (int32_t)g;
+        if (a.indices && !failed) a.indices[margin * kMaxK + s] = (int32_t)g;
       }
     } else {
       uint64_t k[4];
@@ -2644,16 +2643,19 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       float v[4];
       int64_t idx[4];
       decode_keys(k, v, idx);
-      // warm L2 with what the rejection step may gather for these candidates
+      // What the rejection step may gather for these candidates (their noise and draft
+      // probabilities), loaded now for every row, so that the step after the acceptance loop
+      // reads shared memory; the loads overlap the masking and the softmax below.
+      uint16_t gcv[4] = {0, 0, 0, 0};
+      float qcv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         if (idx[j] < 0 || idx[j] >= a.vocab_size) continue;
-        if (!(a.flags & SONIC_FLAG_PHILOX))
-          asm volatile("prefetch.global.L2 [%0];" ::"l"(a.gumbel + slot * a.gumbel_stride + s * a.gumbel_step_stride + idx[j]));
+        if (!(a.flags & SONIC_FLAG_PHILOX)) gcv[j] = a.gumbel[slot * a.gumbel_stride + s * a.gumbel_step_stride + idx[j]];
         if (stochastic_q && s < T - 1) {
           const int64_t qi = slot * a.draft_stride + s * a.draft_step_stride + idx[j];
-          asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.draft_probs +
-                                                         qi * (a.draft_dtype == SONIC_DTYPE_F32 ? 4 : 2)));
+          qcv[j] = a.draft_dtype == SONIC_DTYPE_F32 ? ((const float*)a.draft_probs)[qi]
+                                                    : bf2f(((const uint16_t*)a.draft_probs)[qi]);
         }
       }
       const float vmax = __shfl_sync(kFull, v[0], 0);
@@ -2667,12 +2669,18 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
         const float p = dexp(ls[j]);
         sm.prob[s][i] = p;
         sm.cand[s][i] = (int32_t)idx[j];
-        if (a.values) a.values[(margin + s) * kMaxK + i] = p;
-        if (a.indices) a.indices[(margin + s) * kMaxK + i] = (int32_t)idx[j];
+        sm.gc[s][i] = gcv[j];
+        sm.qc[s][i] = qcv[j];
+        if (a.values && !failed) a.values[(margin + s) * kMaxK + i] = p;
+        if (a.indices && !failed) a.indices[(margin + s) * kMaxK + i] = (int32_t)idx[j];
       }
     }
   }
   __syncthreads();
+  if (failed) {
+    if (tid == 0) ws.tickets[b] = 0;
+    return;
+  }
   if (warp != 0) return;
 
   // ---- chain verification (verify.py:244-434), one warp ----
@@ -2736,9 +2744,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       else if (!stochastic_draft)
         rr = (pos[j] == sm.drafted[accepted]) ? 0.0f : sc;
       else {
-        const int64_t qi = slot * a.draft_stride + accepted * a.draft_step_stride + pos[j];
-        const float q = a.draft_dtype == SONIC_DTYPE_F32 ? ((const float*)a.draft_probs)[qi]
-                                                         : bf2f(((const uint16_t*)a.draft_probs)[qi]);
+        const float q = sm.qc[accepted][i];
         rr = __fsub_rn(sc, q);
         rr = rr < 0.0f ? 0.0f : (rr > 1.0f ? 1.0f : rr);
       }
@@ -2746,7 +2752,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
                           : (flags & SONIC_FLAG_PHILOX)
                                 ? philox_log_exponential(a.philox_seed, a.philox_offset + accepted, (uint32_t)slot,
                                                          (uint32_t)pos[j])
-                                : bf2f(a.gumbel[slot * a.gumbel_stride + accepted * a.gumbel_step_stride + pos[j]]);
+                                : bf2f(sm.gc[accepted][i]);
       score[j] = __fsub_rn(dlog(rr), g);
     }
     const int sel = warp_argmax128(score, lane);
