@@ -2565,8 +2565,8 @@ struct MsSmem {
   float qd[MS_MAX_STEPS];  // draft probability of each drafted token (stochastic drafts)
   float prob[MS_MAX_STEPS][kMaxK];
   int32_t cand[MS_MAX_STEPS][kMaxK];
-  float qc[MS_MAX_STEPS][kMaxK];     // draft probability of each candidate (stochastic drafts)
-  uint16_t gc[MS_MAX_STEPS][kMaxK];  // rejection noise of each candidate (buffered noise)
+  float score[MS_MAX_STEPS][kMaxK];  // residual-draw score of each candidate, were the chain to stop at the row
+  float lz[MS_MAX_STEPS][kMaxK];     // log-probability of each candidate (top-Z outputs)
   int64_t gsel[MS_MAX_STEPS];
 };
 
@@ -2643,9 +2643,9 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       float v[4];
       int64_t idx[4];
       decode_keys(k, v, idx);
-      // What the rejection step may gather for these candidates (their noise and draft
-      // probabilities), loaded now for every row, so that the step after the acceptance loop
-      // reads shared memory; the loads overlap the masking and the softmax below.
+      // What the residual draw needs of these candidates (their noise and draft probabilities),
+      // loaded now for every row: the loads overlap the masking and the softmax below, and the
+      // row's scores are ready when the acceptance loop ends.
       uint16_t gcv[4] = {0, 0, 0, 0};
       float qcv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
@@ -2663,14 +2663,38 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
       if (ind & 0x380) warp_masking(mp, ind, v, vmax, lane, ev);
       float ls[4];
       warp_log_softmax(v, vmax, ls);
+      const bool want_z = a.max_top_logprobs > 0 && (ind & 0x400) && a.top_logprob_values && P.top_logprobs;
+      const int zrow = min(mp.top_logprobs, a.max_top_logprobs);
+      const bool stochastic_draft = a.draft_probs && !(ind & 0x800);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int i = 4 * lane + j;
         const float p = dexp(ls[j]);
         sm.prob[s][i] = p;
         sm.cand[s][i] = (int32_t)idx[j];
-        sm.gc[s][i] = gcv[j];
-        sm.qc[s][i] = qcv[j];
+        if (want_z && i < zrow) sm.lz[s][i] = dlog(p);
+        // rejection_sample (verify.py:157-241) for a chain that stops at this row: the residual
+        // max(p - q, 0) of a stochastic draft, p without the drafted token for a greedy draft,
+        // p itself past the last draft; then log(residual) - noise. A column outside the row
+        // can only come from a workspace that was not zero-filled: it scores -inf.
+        const bool bad = idx[j] < 0 || idx[j] >= a.vocab_size;
+        float rr;
+        if (bad)
+          rr = 0.0f;
+        else if (s == T - 1)
+          rr = p;
+        else if (!stochastic_draft)
+          rr = (idx[j] == sm.drafted[s]) ? 0.0f : p;
+        else {
+          rr = __fsub_rn(p, qcv[j]);
+          rr = rr < 0.0f ? 0.0f : (rr > 1.0f ? 1.0f : rr);
+        }
+        const float g = bad ? 0.0f
+                            : (a.flags & SONIC_FLAG_PHILOX)
+                                  ? philox_log_exponential(a.philox_seed, a.philox_offset + s, (uint32_t)slot,
+                                                           (uint32_t)idx[j])
+                                  : bf2f(gcv[j]);
+        sm.score[s][i] = __fsub_rn(dlog(rr), g);
         if (a.values && !failed) a.values[(margin + s) * kMaxK + i] = p;
         if (a.indices && !failed) a.indices[(margin + s) * kMaxK + i] = (int32_t)idx[j];
       }
@@ -2726,35 +2750,10 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
         if (s == accepted) keep = u <= targets[s];
       if (!keep) break;
     }
-    // rejection_sample (verify.py:157-241)
+    // rejection_sample (verify.py:157-241): the accepted row's scores, computed in the merge
     float score[4];
-    int32_t pos[4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = 4 * lane + j;
-      const float sc = sm.prob[accepted][i];
-      pos[j] = sm.cand[accepted][i];
-      // a column outside the row can only come from a workspace that was not zero-filled
-      const bool bad = pos[j] < 0 || pos[j] >= a.vocab_size;
-      float rr;
-      if (bad)
-        rr = 0.0f;
-      else if (accepted == T - 1)
-        rr = sc;
-      else if (!stochastic_draft)
-        rr = (pos[j] == sm.drafted[accepted]) ? 0.0f : sc;
-      else {
-        const float q = sm.qc[accepted][i];
-        rr = __fsub_rn(sc, q);
-        rr = rr < 0.0f ? 0.0f : (rr > 1.0f ? 1.0f : rr);
-      }
-      const float g = bad ? 0.0f
-                          : (flags & SONIC_FLAG_PHILOX)
-                                ? philox_log_exponential(a.philox_seed, a.philox_offset + accepted, (uint32_t)slot,
-                                                         (uint32_t)pos[j])
-                                : bf2f(sm.gc[accepted][i]);
-      score[j] = __fsub_rn(dlog(rr), g);
-    }
+    for (int j = 0; j < 4; ++j) score[j] = sm.score[accepted][4 * lane + j];
     const int sel = warp_argmax128(score, lane);
     token = sm.cand[accepted][sel];
     const float psel = sm.prob[accepted][sel];
@@ -2772,8 +2771,7 @@ __global__ void __launch_bounds__(NT) ms_verify_kernel(const SonicMultistepArgs 
           for (int j = 0; j < 4; ++j) {
             const int i = 4 * lane + j;
             if (i < z) {
-              store_float(a.top_logprob_values, a.logprobs_dtype, (margin + s) * a.top_stride + i,
-                          dlog(sm.prob[s][i]));
+              store_float(a.top_logprob_values, a.logprobs_dtype, (margin + s) * a.top_stride + i, sm.lz[s][i]);
               a.top_logprob_tokens[(margin + s) * a.top_stride + i] = sm.cand[s][i];
             }
           }
