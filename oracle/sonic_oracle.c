@@ -336,7 +336,14 @@ static void cumulative_masking(const SonicSamplingParams* P, int64_t slot, uint1
     float e[MAXK], lad[MAXK];
     for (int i = 0; i < MAXK; ++i) e[i] = ox_exp(v[i] - maximum);
     ladder128(e, lad);
-    float scale = lad[MAXK - 1] * bf2f(P->top_p[slot]);
+    /* ops/base.py:81-84 scales the prefix sum's last element. The reference's prefix sums of
+       these non-negative terms never decrease, so that element is also their maximum; this
+       order's scan can end an ulp below an earlier prefix past the last nonzero term (the
+       lanes' totals are grouped differently), so the maximum is taken. */
+    float total = lad[0];
+    for (int i = 1; i < MAXK; ++i)
+      if (lad[i] > total) total = lad[i];
+    float scale = total * bf2f(P->top_p[slot]);
     for (int i = 0; i < MAXK; ++i)
       if (!(lad[i] <= scale || i == 0)) v[i] = -INFINITY;
   }

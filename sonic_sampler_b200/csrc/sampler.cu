@@ -566,7 +566,12 @@ __device__ __forceinline__ bool warp_masking(const MaskParams& M, uint32_t ind, 
 #pragma unroll
     for (int j = 0; j < 4; ++j) e[j] = dexp(__fsub_rn(v[j], maximum));
     warp_ladder128(e, lad, lane);
-    const float total = __shfl_sync(kFull, lad[3], 31);
+    // ops/base.py:81-84 scales the prefix sum's last element, which is also the maximum of the
+    // reference's never-decreasing prefix sums; this scan can end an ulp below an earlier prefix
+    // past the last nonzero term (the lane totals are grouped differently), so take the maximum
+    float total = fmaxf(fmaxf(lad[0], lad[1]), fmaxf(lad[2], lad[3]));
+#pragma unroll
+    for (int d = 16; d >= 1; d >>= 1) total = fmaxf(total, __shfl_xor_sync(kFull, total, d));
     const float scale = __fmul_rn(total, bf2f(M.top_p));
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -1078,10 +1083,26 @@ __device__ __forceinline__ void row_smem_init(RowSmem<K, QC>& st, unsigned long 
   for (int i = 0; i < NW; ++i) st.v16[i] = st.vlm[i] = __int_as_float(0xff800000);
 }
 
-// Loads of one group of 8 columns per lane (`c` = first column of this lane).
+// Drafted tokens counted as decoded (ops/prologue.py:175-193) for columns whose aux values were
+// gathered through a draft-to-target table: the drafted tokens are target ids, so they are
+// matched against the columns' target ids `col` (the caller counts them by position otherwise).
+__device__ __forceinline__ void add_drafted(Raw8& raw, const int64_t (&col)[VPT], int nvalid, const int32_t* toks,
+                                            int ntok) {
+  for (int t = 0; t < ntok; ++t) {
+    const int64_t d = toks[t];
+#pragma unroll
+    for (int j = 0; j < VPT; ++j)
+      if (j < nvalid) raw.d[j] += (col[j] == d);
+  }
+}
+
+// Loads of one group of 8 columns per lane (`c` = first column of this lane). With a
+// draft-to-target table (INDIRECT) the `ntok` drafted tokens `toks` are added to the decode
+// counts here, by target id.
 template <int MODE, bool INDIRECT>
 __device__ __forceinline__ void load_group(const SonicSingularArgs& a, const RowConsts& rc, int64_t slot,
-                                           int64_t gslot, const uint16_t* xrow, int64_t c, int nvalid, Raw8& raw) {
+                                           int64_t gslot, const uint16_t* xrow, int64_t c, int nvalid, Raw8& raw,
+                                           const int32_t* toks = nullptr, int ntok = 0) {
   constexpr int AM = INDIRECT ? kScalar : MODE;
   load_x8<MODE>(xrow, c, nvalid, raw.x);
   raw.g = 0xffu;
@@ -1094,6 +1115,7 @@ __device__ __forceinline__ void load_group(const SonicSingularArgs& a, const Row
     }
     load_aux8<AM>(a.params, rc, slot, col, nvalid, raw);
     if (rc.nd.g) raw.g = load_g8<AM>(a.params, gslot, col, nvalid);
+    if (INDIRECT) add_drafted(raw, col, nvalid, toks, ntok);
   }
 }
 
@@ -1448,10 +1470,10 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       greedy_group(raw, c, nvalid);
       return;
     }
-    if (rc.nd.proc && ntok) {
+    if (!INDIRECT && rc.nd.proc && ntok) {
 #pragma unroll
       for (int j = 0; j < VPT; ++j) {
-        const int64_t col = INDIRECT ? -1 : c + j + shard;
+        const int64_t col = c + j + shard;
         for (int s = 0; s < ntok; ++s) raw.d[j] += (st.toks[s] == col);
       }
     }
@@ -1489,7 +1511,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       uint32_t need = 0;
 #pragma unroll
       for (int j = 0; j < VPT; ++j) need |= (uint32_t)((raw.d[j] | (rc.nd.ctx ? raw.c[j] : 0)) != 0) << j;
-      for (int t = 0; t < ntok; ++t) {
+      for (int t = 0; t < (INDIRECT ? 0 : ntok); ++t) {
         const int64_t dl = (int64_t)st.toks[t] - (c + shard);
         if (dl >= 0 && dl < nvalid) need |= 1u << dl;
       }
@@ -1500,7 +1522,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       for (int j = 0; j < VPT; ++j) {
         if ((bits >> j) & 1u) {
           int32_t dj = raw.d[j];
-          for (int t = 0; t < ntok; ++t) dj += (st.toks[t] == c + j + shard);
+          for (int t = 0; t < (INDIRECT ? 0 : ntok); ++t) dj += (st.toks[t] == c + j + shard);
           const uint32_t h = repetition_one(half_of(v, j), dj, rc.nd.ctx ? raw.c[j] : 0, rc);
           v[j >> 1] = (j & 1) ? ((v[j >> 1] & 0xffffu) | (h << 16)) : ((v[j >> 1] & 0xffff0000u) | h);
         }
@@ -1688,6 +1710,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
         }
         load_aux8<kScalar>(a.params, rc, slot, col, nv, raw);
         if (rc.nd.g) raw.g = load_g8<kScalar>(a.params, gslot, col, nv);
+        add_drafted(raw, col, nv, st.toks, ntok);
       }
       if (rdrow) {
         const unsigned char* dp = sp + sg_d + warp * (GROUP * 4) + lane * 32;
@@ -1710,7 +1733,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       if (rgrow) raw.g = sp[sg_g + warp * (GROUP / 8) + lane];
       pc.add(PW_LOADS, tl);
     } else {
-      load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, c, nv, raw);
+      load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, c, nv, raw, st.toks, ntok);
     }
     process_group(raw, c, nv, k);
     if (staged) {
@@ -1820,7 +1843,7 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
       tq = false;  // the exact path pushes final keys
       for (int gg = warp; gg < ngroups; gg += NW) {
         Raw8 raw;
-        load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, gcol(gg), gvalid(gg), raw);
+        load_group<DM, INDIRECT>(a, rc, slot, gslot, xrow, gcol(gg), gvalid(gg), raw, st.toks, ntok);
         wtk_adopt(w, &st.cut, lane);
         exact_group(raw, gcol(gg), gvalid(gg));
         absorb_if_full();

@@ -386,6 +386,32 @@ def test_slot_mapping_int64_d2t_int32(dev):
     assert_selection_equal(sel, ref, kw, kh)
 
 
+def test_d2t_drafting_counts_drafted_tokens_by_target_id(dev):
+    """A drafting step after the first (drafted tokens counted as decoded, ops/prologue.py:175-193)
+    through a draft-to-target table: the drafted tokens are target ids and must be matched
+    against each column's target id, on the fast path (stochastic rows) and the exact path
+    (greedy rows). The drafted tokens are the target ids of each row's best draft columns, so
+    the repetition penalties change which candidates survive. Tokens, logprobs and draft
+    probabilities match the oracle bit for bit."""
+    vd, vt, slots, gamma = 6000, 9000, 12, 3
+    b = _params(dev, slots, vt, seed=5, top_logprobs=2)
+    ind = b.flags.target.cpu().to(torch.int32)
+    ind[::3] = (ind[::3] & 0x3F) | 0x40  # some greedy rows (exact path)
+    b.flags.packed[:, 0] = ind.to(torch.uint16).to(dev)
+    x = workloads.peaked_logits(7, vd, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=5)
+    d2t = torch.randperm(vt, generator=torch.Generator().manual_seed(5))[:vd].to(I32).to(dev)
+    sm = torch.tensor([11, 3, 0, 7, 5, 9, 1], dtype=torch.int64, device=dev)
+    drafted = torch.zeros(slots, gamma, dtype=I32, device=dev)
+    best = d2t[x.float().topk(gamma, dim=-1).indices]  # [7, gamma] target ids of the best columns
+    drafted[sm] = best.to(I32)
+    probs = torch.zeros(slots, vt, dtype=BF16, device=dev)
+    kw = buffer_kwargs(b)
+    sel, ref, kw, kh = run_singular(x, block_n=1024, slot_mapping=sm, d2t_mapping=d2t, target_vocab=vt,
+                                    lookahead=gamma, drafted_tokens=drafted, return_probabilities=True,
+                                    draft_probabilities=probs, return_logprobs=True, **kw)
+    assert_selection_equal(sel, ref, kw, kh)
+
+
 def test_top_logprobs_request_above_capacity_is_clamped(dev):
     b = _params(dev, 4, 4096, seed=5, top_logprobs=9)
     x = workloads.peaked_logits(4, 4096, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=5)

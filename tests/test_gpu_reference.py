@@ -325,3 +325,64 @@ def test_config4_chain_matches_reference(ref, dev):
     assert torch.equal(to, oo)
     for x, y in zip(results["ours"], results["ours_i32"]):
         assert torch.equal(x, y)
+
+
+# ----------------------------------------------------------------------------------------
+# stochastic drafting: UnshardedFusedSingular.drafting with the draft-probability output
+# ----------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("case", ["draft_vocab", "d2t_slots"])
+def test_stochastic_drafting_matches_reference(ref, dev, case):
+    """Two drafting steps of stochastic rows with every processor, through the modular
+    `drafting` call of both implementations; the second step counts the first step's drafted
+    tokens as decoded. `draft_vocab`: 64 slots drafting over their own 32000-token vocabulary.
+    `d2t_slots`: 128 requests in 256 slots drafting over 32000 draft tokens mapped into a
+    128256-token target vocabulary by an int32 table (the reference needs int32), the buffers
+    and the probability output indexed by target id. Tokens must match bit for bit; the draft
+    probabilities (bf16 in the reference) must be round-to-nearest bf16 values of our fp32
+    probabilities within 1e-5."""
+    from sonic_sampler_b200.interface import UnshardedFusedSingular
+
+    gamma, draft_vocab = 3, 32000
+    if case == "draft_vocab":
+        slots, active, target_vocab = 64, 64, None
+        sm, d2t = None, None
+    else:
+        slots, active, target_vocab = 256, 128, 128256
+        g = torch.Generator().manual_seed(71)
+        sm = torch.randperm(slots, generator=g)[:active].to(I32).to(dev)
+        d2t = torch.randperm(target_vocab, generator=g)[:draft_vocab].to(I32).to(dev)
+    bvocab = target_vocab or draft_vocab
+    base = workloads.sampling_buffers(slots, gamma + 1, bvocab, dev, 72, workloads.config2_params(slots, 73))
+    logits = [workloads.peaked_logits(active, draft_vocab, sigma=3.0, peaks=4, lift=12.0, device=dev, seed=74 + t)
+              for t in range(2)]
+    rows = sm.long() if sm is not None else torch.arange(active, device=dev)
+    out = {}
+    for who, pdt in (("theirs", BF16), ("ours", BF16), ("ours_f32", F32)):
+        b = base.to(dev)
+        if who == "theirs":
+            with torch.device(dev):
+                drafter = ref.UnshardedFusedSingular.initialize(draft_vocab, batch_size=active, lookahead=gamma)
+        else:
+            drafter = UnshardedFusedSingular.initialize(draft_vocab, batch_size=active, lookahead=gamma)
+        table = torch.zeros(slots, gamma + 1, dtype=I32, device=dev)  # drafted tokens per slot
+        probs, toks = [], []
+        for t in range(2):
+            p = torch.zeros(slots, bvocab, dtype=pdt, device=dev)
+            sel = drafter.drafting(logits[t], b, timestep=t, tokens=table if t else None, probabilities=p,
+                                   slot_mapping=sm, d2t_mapping=d2t, target_vocab=target_vocab)
+            table[rows, t] = sel.tokens[:, 0]
+            toks.append(sel.tokens[:, 0].clone())
+            probs.append(p)
+        out[who] = (torch.stack(toks).cpu(), torch.stack(probs).cpu())
+    torch.cuda.synchronize()
+    (tt, tp), (ot, op), (_, fp) = out["theirs"], out["ours"], out["ours_f32"]
+    ok = lp_within(tp, fp)
+    report(f"stochastic drafting {case}", rows=active, token_mismatch=int((tt != ot).sum()),
+           probability_outside_1e5=int((~ok).sum()),
+           probability_bf16_bits_differ=int((tp.view(torch.int16) != op.view(torch.int16)).sum()),
+           nonzero_probabilities=int((tp != 0).sum()))
+    assert int((tp != 0).sum()) > 0
+    assert torch.equal(tt, ot)
+    assert bool(ok.all())
