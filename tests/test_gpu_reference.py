@@ -250,6 +250,67 @@ def test_config3_matches_reference(ref, dev, varlen, q_dtype):
     assert bool(lp_ok.all()) and torch.equal(zt_t, zt_o) and bool(zl_ok.all())
 
 
+def test_multistep_mixed_greedy_slots_matches_reference(ref, dev):
+    """Config-3 shapes (fixed layout, bf16 draft probabilities) with every third request
+    greedy and the requests mapped to slots by a permutation: greedy and stochastic
+    verification side by side. Offsets, tokens and decode counts bit for bit; the stochastic
+    requests' stage-2 candidate ids bit for bit and probabilities within 1e-5, their logprobs
+    and top-20 within 1e-5 (neither implementation writes logprobs for greedy requests)."""
+    from sonic_sampler_b200.interface.functional.multistep import fused_multistep
+
+    c = workloads.config3(dev, seed=13, varlen=False)
+    gamma, vocab = c["gamma"], 128256
+    batch = c["tokens"].size(0)
+    sm = torch.randperm(batch, generator=torch.Generator().manual_seed(14)).to(I32).to(dev)
+    base = c["buffers"]
+    ind = base.flags.packed[:, 0].to(I32)
+    ind[::3] = (ind[::3] & 0x3F) | 0x40
+    base.flags.packed[:, 0] = ind.to(torch.uint16)
+    base.flags.target_host = [int(v) for v in ind.tolist()]
+    q = c["probabilities"].to(BF16)
+    rows = batch * (gamma + 1)
+    out = {}
+    for who in ("theirs", "ours", "ours_f32"):
+        b = base.to(dev)
+        vals = torch.zeros(rows, 128, dtype=F32, device=dev)
+        idx = torch.full((rows, 128), -1, dtype=I32, device=dev)
+        kw = dict(lookahead=gamma, max_top_logprobs=20, return_logprobs=True, update_counts=True,
+                  draft_probabilities=q, block_n=4096, values=vals, indices=idx, slot_mapping=sm,
+                  **_multistep_kwargs(b))
+        if who == "theirs":
+            v = ref.fused_multistep(c["logits"], b.flags.target, c["tokens"].clone(), **kw)
+        else:
+            if who == "ours_f32":
+                kw["logprobs_dtype"] = F32
+            v = fused_multistep(c["logits"], b.flags.target, c["tokens"].clone(), **kw)
+        out[who] = (v, vals, idx, b)
+    torch.cuda.synchronize()
+    (tv, tvals, tidx, tb), (ov, ovals, oidx, ob), (fv, _, _, _) = out["theirs"], out["ours"], out["ours_f32"]
+    off_t, off_o = tv.offsets.cpu().view(-1), ov.offsets.cpu().view(-1)
+    greedy = (ind.cpu()[sm.long().cpu()] & 0x40).bool()  # per request
+    stoch_rows = (~greedy).repeat_interleave(gamma + 1)
+    tok_bad = (tv.tokens.cpu() != ov.tokens.cpu())
+    cnt_bad = (tb.repetition.counts.decode != ob.repetition.counts.decode).any(dim=1).cpu()
+    idx_bad = ((tidx != oidx).any(dim=1).cpu() & stoch_rows)
+    prob_bad = (((tvals - ovals).abs() > TOL).any(dim=1).cpu() & stoch_rows)
+    m = (torch.arange(gamma + 1)[None, :] <= off_t[:, None]) & ~greedy[:, None]
+    lp_t, lp_f = tv.logprobs.selected.cpu()[m], fv.logprobs.selected.cpu()[m]
+    zt_t, zt_o = tv.logprobs.top_k.tokens.cpu()[m], ov.logprobs.top_k.tokens.cpu()[m]
+    zl_t, zl_f = tv.logprobs.top_k.logprobs.cpu()[m], fv.logprobs.top_k.logprobs.cpu()[m]
+    lp_ok, zl_ok = lp_within(lp_t, lp_f), lp_within(zl_t, zl_f)
+    report("multistep mixed greedy + slots", requests=batch, greedy_requests=int(greedy.sum()),
+           offset_mismatch=int((off_t != off_o).sum()), token_mismatch=int(tok_bad.sum()),
+           count_rows_mismatch=int(cnt_bad.sum()), stage2_index_rows_mismatch=int(idx_bad.sum()),
+           stage2_prob_rows_outside_1e5=int(prob_bad.sum()), logprob_outside_1e5=int((~lp_ok).sum()),
+           topz_token_mismatch=int((zt_t != zt_o).sum()), topz_logprob_outside_1e5=int((~zl_ok).sum()))
+    assert int(greedy.sum()) > 0 and int((~greedy).sum()) > 0
+    assert torch.equal(off_t, off_o)
+    assert not tok_bad.any()
+    assert not cnt_bad.any()
+    assert not idx_bad.any() and not prob_bad.any()
+    assert bool(lp_ok.all()) and torch.equal(zt_t, zt_o) and bool(zl_ok.all())
+
+
 def test_reference_rejects_fp32_draft_probabilities(ref, dev):
     """The reference cannot verify with fp32 draft probabilities on the GPU: under Triton 3.6
     its `verify_drafted` (ops/verify.py:134-147) multiplies the bf16 uniforms by the fp32
