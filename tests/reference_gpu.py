@@ -48,6 +48,7 @@ def load():
     iface = importlib.import_module("sonic_sampler.interface")
     fsing = importlib.import_module("sonic_sampler.interface.functional.singular")
     fmult = importlib.import_module("sonic_sampler.interface.functional.multistep")
+    copy = importlib.import_module("sonic_sampler.ops.copy")
 
     class Ref:
         UnshardedFusedSingular = iface.UnshardedFusedSingular
@@ -55,5 +56,6 @@ def load():
         UnshardedBoundedTopK = iface.UnshardedBoundedTopK
         fused_singular = fsing.fused_singular
         fused_multistep = fmult.fused_multistep
+        indexed_copy = copy.indexed_copy
 
     return Ref

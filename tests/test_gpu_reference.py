@@ -447,3 +447,39 @@ def test_stochastic_drafting_matches_reference(ref, dev, case):
     assert int((tp != 0).sum()) > 0
     assert torch.equal(tt, ot)
     assert bool(ok.all())
+
+
+# ----------------------------------------------------------------------------------------
+# noise staging: GumbelNoise.stage_weights (ops/copy.py indexed_copy)
+# ----------------------------------------------------------------------------------------
+
+
+@pytest.mark.parametrize("case", ["config_rows", "odd_rows_duplicates"])
+def test_indexed_copy_matches_reference(ref, dev, case):
+    """The draft noise of the indexed rows whose indicator lacks the greedy bit, copied into the
+    target noise: 128 of 256 slots x 4 steps x 128256 bf16 (the bulk-copy ring), and rows of
+    1001 values with repeated indices (the element-wise kernel). Bit for bit."""
+    from sonic_sampler_b200.ops import indexed_copy
+
+    g = torch.Generator().manual_seed(91)
+    if case == "config_rows":
+        shape, n = (256, 4, 128256), 128
+        indices = torch.randperm(256, generator=g)[:n]
+    else:
+        shape, n = (40, 3, 1001), 30
+        indices = torch.randint(0, 40, (n,), generator=g)
+    source = torch.randn(*shape, generator=g).to(BF16).to(dev)
+    indicator = torch.zeros(shape[0], dtype=torch.uint16)
+    indicator[::2] = 0x40
+    indicator = indicator.to(dev)
+    idx = indices.to(I32).to(dev)
+    theirs = torch.zeros_like(source)
+    ours = torch.zeros_like(source)
+    ref.indexed_copy(source, theirs, idx, indicator)
+    indexed_copy(source, ours, idx, indicator)
+    torch.cuda.synchronize()
+    differ = int((theirs.view(torch.int16) != ours.view(torch.int16)).sum())
+    report(f"indexed_copy {case}", rows=n, elements_differ=differ, rows_copied=int((ours != 0).flatten(1).any(1).sum()))
+    assert differ == 0
+    assert bool((ours != 0).any())
+
