@@ -483,3 +483,89 @@ def test_indexed_copy_matches_reference(ref, dev, case):
     assert differ == 0
     assert bool((ours != 0).any())
 
+
+# ----------------------------------------------------------------------------------------
+# slot population: SamplingBuffers.allocate / update at the full vocabulary
+# ----------------------------------------------------------------------------------------
+
+
+def _ref_state(b) -> dict:
+    """The device-side fields of the reference's SamplingBuffers, cloned."""
+    rep, w = b.repetition, b.weights
+    plain = lambda t: torch.Tensor(t).as_subclass(torch.Tensor).clone()  # noqa: E731
+    return dict(
+        flags=plain(b.flags.packed), temperature=plain(b.temperature), top_p=plain(b.top_p), min_p=plain(b.min_p),
+        top_k=plain(b.top_k), top_logprobs=plain(b.top_logprobs), multiplicative=plain(rep.multiplicative),
+        frequency=plain(rep.frequency), presence=plain(rep.presence), context=plain(rep.counts.context),
+        decode=plain(rep.counts.decode), bias=plain(b.bias), grammar=plain(b.grammar).view(torch.int32),
+        gumbel_target=plain(w.gumbel.target), gumbel_draft=plain(w.gumbel.draft), uniform=plain(w.uniform),
+    )
+
+
+def test_population_matches_reference(ref, dev):
+    """The reference's own SamplingBuffers (core/buffer.py) and ours, on the B200 at the full
+    vocabulary (48 slots, 4 steps, V = 128256), starting from the same state and given the same
+    admissions (prompts up to 1.5 V tokens, logit biases, bitmasks, greedy drafts) and updates
+    (dense count rows), with CUDA generators seeded alike: every field, the noise included, bit
+    for bit after each call (bias rows only where the BIAS bit is set: the reference copies its
+    pinned mirror's stale contents for the others). Bitmasks go only with identity-prefix
+    positions, where the reference's slot-indexed reading of them agrees with ours."""
+    from sonic_sampler.core.buffer import SamplingBuffers as RefBuffers  # noqa: E402 (reference, on sys.path)
+    from tests.test_populate import assert_state, buffers_from_state
+
+    B, T, V = 48, 4, 128256
+    W = (V + 31) // 32
+    torch.manual_seed(17)
+    theirs = RefBuffers.default(B, T, V, device=dev)
+    ours = buffers_from_state(_ref_state(theirs), device=dev)
+    g = torch.Generator().manual_seed(18)
+
+    def params(n):
+        return dict(
+            multiplicative=[float(x) for x in (torch.rand(n, generator=g) * 0.6 + 0.7)],
+            frequency=[float(x) for x in (torch.rand(n, generator=g) - 0.5)],
+            presence=[float(x) for x in (torch.rand(n, generator=g) * 0.4)],
+            temperature=[float(x) for x in (torch.rand(n, generator=g) + 0.4)],
+            top_k=[(128, 20, 1, 64)[int(i)] for i in torch.randint(0, 4, (n,), generator=g)],
+            top_p=[float(x) for x in (torch.rand(n, generator=g) * 0.3 + 0.7)],
+            min_p=[(0.0, 0.05)[int(i)] for i in torch.randint(0, 2, (n,), generator=g)],
+            top_logprobs=[int(i) for i in torch.randint(0, 6, (n,), generator=g)],
+            biases=[None if j % 3 == 1 else {int(t): float(torch.randn(1, generator=g)) * 2
+                                             for t in torch.randperm(V, generator=g)[: 2 + j % 16].tolist()}
+                    for j in range(n)],
+            greedy_drafts=[bool(j % 2) for j in range(n)],
+        )
+
+    def masks(n, full):
+        out = []
+        for j in range(n):
+            rows = T if (full and j % 4 == 0) else 1
+            m = torch.randint(-2**31, 2**31 - 1, (rows, W), generator=g, dtype=torch.int64).to(torch.int32)
+            out.append(None if j % 2 else (m[0] if rows == 1 else m))
+        return out
+
+    plan = [("allocate", torch.randperm(B, generator=g)[:20].tolist(), False),
+            ("allocate", list(range(12)), True),
+            ("update", torch.randperm(B, generator=g)[:16].tolist(), False),
+            ("update", None, True)]
+    for k, (kind, positions, grammar) in enumerate(plan):
+        n = len(positions) if positions else B
+        kw = params(n)
+        if grammar:
+            kw["bitmasks"] = masks(n, full=(kind == "update"))
+        if kind == "allocate":
+            kw["encodings"] = [torch.randint(0, V, (int(torch.randint(1, 3 * V // 2, (1,), generator=g)),), generator=g)
+                               for _ in range(n)]
+        else:
+            kw["counts"] = [(torch.randint(0, 9, (V,), generator=g, dtype=torch.int32),
+                             torch.randint(0, 5, (V,), generator=g, dtype=torch.int32)) for _ in range(n)]
+            kw["target_gumbel"] = [None] * n
+        kw["positions"] = positions
+        seed = 2000 + 17 * k
+        getattr(theirs, kind)(generator=torch.Generator(dev).manual_seed(seed), **kw)
+        getattr(ours, kind)(generator=torch.Generator(dev).manual_seed(seed), **kw)
+        torch.cuda.synchronize()
+        want = _ref_state(theirs)
+        assert_state(ours, want, f"population call {k} ({kind})")
+        report(f"population call {k} ({kind})", slots=n, fields_equal=1)
+
