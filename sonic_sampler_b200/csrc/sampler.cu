@@ -2184,9 +2184,9 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint32_t phase = 0;
   for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
-    const int nv = gvalid(g);
-    uint32_t x[8];
     const bool staged = k < nchunks;
+    uint32_t x[8];
+    const int nv = staged ? PVPT : gvalid(g);  // ring groups are whole
     if (staged) {
       const long long tw = pc.now();
       if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
@@ -2207,7 +2207,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       const uint32_t m01 = bf2_max(bf2_max(x[0], x[1]), bf2_max(x[2], x[3]));
       const uint32_t m23 = bf2_max(bf2_max(x[4], x[5]), bf2_max(x[6], x[7]));
       lmv = bf2_max(lmv, bf2_max(m01, m23));
-      if (k == 1 || k == 3 || k == 7 || k == 15 || k == 31 || k == 63) {
+      if (k <= 63 && k > 0 && (k & (k + 1)) == 0) {  // k = 1, 3, 7, 15, 31, 63
         const uint32_t lo = lmv & 0xffffu, hi = lmv >> 16;
         const uint32_t h = enc16(lo) >= enc16(hi) ? lo : hi;
         lane_max_publish((h & 0x7fffu) <= 0x7f80u ? enc16(h) << 16 : 0u, st.vlm, warp, lane, final_of, mm);
