@@ -1681,9 +1681,9 @@ __global__ void __launch_bounds__(NT) singular_kernel(const SonicSingularArgs a,
   // the remaining groups: standard ring chunks, then direct loads
   for (int k = 0, g = (wide ? wg * NW * nck : 0) + warp; g < ngroups && !werr; ++k, g += NW) {
     const int64_t c = gcol(g);
-    const int nv = gvalid(g);
-    Raw8 raw;
     const bool staged = k < nchunks;
+    const int nv = staged ? VPT : gvalid(g);  // ring groups are whole
+    Raw8 raw;
     if (staged) {
       const long long tw = pc.now();
       if (!ring_wait(&st.bars[stage], phase, &st.abort)) {
