@@ -2088,6 +2088,7 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
     w.qn += total;
     pc.add(PW_PUSHPATH, tpp);
   };
+  int adopt_tick = 0;
   auto process16 = [&](const uint32_t (&x)[8], int64_t c, int nvalid, bool exact) {
     const long long tp = pc.now();
     pc.count(PW_GROUPS, 1);
@@ -2132,7 +2133,8 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
       pc.add(PW_PROCESS, tp);
       return;
     }
-    wtk_adopt(w, &st.cut, lane);
+    // the CTA cut of the other warps, adopted every other group (a stale cut only admits more)
+    if (exact || (++adopt_tick & 1)) wtk_adopt(w, &st.cut, lane);
     uint32_t m = 0;
     if (rc.fast && !exact) {
       const uint32_t lo[4] = {x[0], x[1], x[2], x[3]}, hi[4] = {x[4], x[5], x[6], x[7]};
@@ -2182,8 +2184,9 @@ __global__ void __launch_bounds__(NT, MINB) plain_kernel(const SonicSingularArgs
   uint32_t lmv = 0xff80ff80u;
   int stage = 0;
   uint32_t phase = 0;
-  for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW) {
-    const int64_t c = gcol(g);
+  int64_t cg = gcol(warp);  // the lane's first column of group g, advanced with g
+  for (int k = 0, g = warp; g < ngroups && !werr; ++k, g += NW, cg += (int64_t)NW * PGROUP) {
+    const int64_t c = cg;
     const bool staged = k < nchunks;
     uint32_t x[8];
     const int nv = staged ? PVPT : gvalid(g);  // ring groups are whole
